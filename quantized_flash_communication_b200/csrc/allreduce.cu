@@ -1,0 +1,564 @@
+// Fused quantized all-reduce over peer memory (NVLink 5 / NVSwitch): one kernel per call.
+//
+// Capability of the reference's flash_all_reduce (communication.py:7-97): the two-step
+// Flash-Communication all-reduce (quantize -> reduce-scatter -> dequant-sum -> requantize
+// -> all-gather -> dequantize) with INT8 / INT6 (INT4 + INT8) / INT4 / 16-bit payloads,
+// asymmetric or symmetric groups.  The reference runs it as ~7W+10 kernel launches, six
+// NCCL collectives and two host synchronisations per call; here it is a single launch:
+//
+//   phase 1  every CTA quantizes its 256-element units of every chunk in registers and
+//            stores the packed codes + per-group metadata straight into the chunk owner's
+//            reduce-scatter slot (plain st.global to the peer's mapped buffer), then
+//            publishes a per-(block, source) flag with a release store;
+//   phase 2  the owner CTA waits for the W flags of its block, dequant-sums the W
+//            contributions in fp32, requantizes, pushes the result into every peer's
+//            all-gather slot and writes its own chunk of the output;
+//   phase 3  after the all-gather flags, it dequantizes the other chunks into the output.
+//
+// CTA b of every rank handles the same unit indices, so each CTA only ever waits for
+// CTA b of the other ranks: no grid-wide barrier, and the grid is capped at the number
+// of co-resident CTAs so that every waited-for CTA is running.  Each wait is bounded by
+// %globaltimer; on expiry the CTA records the failure in a host-mapped status word and
+// returns.  A one-shot variant (every rank gathers every rank's quantized tensor and
+// sums locally, one round trip, one quantization) serves small, latency-bound messages.
+//
+// Epochs live in device memory (one counter per algorithm and block, advanced by the
+// kernel itself), so the launch is safe to capture in a CUDA graph and replay.
+//
+// Single-GPU emulation: with gridDim.y == W, block row y plays rank y, and every "peer"
+// buffer is a separate local allocation.  All W ranks then run inside one launch, which
+// lets the multi-rank protocol be exercised on one GPU.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAException.h>
+
+#include <memory>
+
+#include "common.cuh"
+#include "workspace.h"
+
+namespace qfc {
+
+struct ARParams {
+  const void* in[kMaxRanks];
+  void* out[kMaxRanks];
+  char* base[kMaxRanks];
+  uint32_t* epochs[kMaxRanks];
+  KernelStatus* status;
+  int64_t n;       // elements
+  int64_t chunk;   // two-shot: elements per chunk; one-shot: n rounded up to 256
+  int64_t rs_off, ag_off, os_off, os_bytes;
+  int64_t slot1, slot2;  // slot strides in bytes (one-shot uses slot1)
+  int64_t pay1, pay2;    // payload bytes at the head of a slot; metadata follows
+  uint64_t timeout_ns;
+  int world, rank, gs, meta_fp32, sym, quantize_local;
+};
+
+namespace {
+
+QFC_DEV uint32_t* flag_at(char* base, int phase, int block, int src) {
+  return reinterpret_cast<uint32_t*>(base) + ((int64_t)(phase * kMaxBlocks + block) * kMaxRanks + src);
+}
+
+// One lane's 8 elements in wire form, plus its group's parameters.
+struct Enc8 {
+  uint4 a, b;
+  float s, z;
+};
+
+template <int P>
+QFC_DEV void quantize8(const float (&v)[8], int lpg, bool sym, uint32_t (&c)[8], float& s, float& z) {
+  float mn = v[0], mx = v[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    mn = fminf(mn, v[i]);
+    mx = fmaxf(mx, v[i]);
+  }
+  for (int off = lpg >> 1; off > 0; off >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(QFC_FULL_MASK, mn, off));
+    mx = fmaxf(mx, __shfl_xor_sync(QFC_FULL_MASK, mx, off));
+  }
+  float inv;
+  if (sym) QMath<P, true>::params(mn, mx, s, inv, z);
+  else QMath<P, false>::params(mn, mx, s, inv, z);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = QMath<P, false>::code(v[i], inv, z);
+}
+
+template <int P, typename WT>
+QFC_DEV Enc8 encode8(const float (&v)[8], int lpg, bool sym) {
+  Enc8 e;
+  e.a = make_uint4(0, 0, 0, 0);
+  e.b = make_uint4(0, 0, 0, 0);
+  e.s = 1.f;
+  e.z = 0.f;
+  if constexpr (P == 16) {
+    if constexpr (sizeof(WT) == 2) {
+      e.a = Vec8IO<WT>::pack(v);
+    } else {
+      e.a = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+      e.b = make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]), __float_as_uint(v[7]));
+    }
+  } else {
+    uint32_t c[8];
+    quantize8<P>(v, lpg, sym, c, e.s, e.z);
+    if constexpr (P == 8) {
+      const uint2 u = codes8_to_u2(c);
+      e.a.x = u.x;
+      e.a.y = u.y;
+    } else {
+      e.a.x = codes8_to_int4(c);
+    }
+  }
+  return e;
+}
+
+template <int P, typename WT>
+QFC_DEV void store8(char* slot, char* meta, int64_t loc, const Enc8& e, bool leader, int gs, int meta_fp32) {
+  if constexpr (P == 16) {
+    if constexpr (sizeof(WT) == 2) {
+      *reinterpret_cast<uint4*>(slot + loc * 2) = e.a;
+    } else {
+      uint4* d = reinterpret_cast<uint4*>(slot + loc * 4);
+      d[0] = e.a;
+      d[1] = e.b;
+    }
+  } else {
+    if constexpr (P == 8) *reinterpret_cast<uint2*>(slot + loc) = make_uint2(e.a.x, e.a.y);
+    else *reinterpret_cast<uint32_t*>(slot + (loc >> 1)) = e.a.x;
+    if (leader) {
+      const int64_t g = loc / gs;
+      if (meta_fp32) *reinterpret_cast<float2*>(meta + g * 8) = make_float2(e.s, e.z);
+      else *reinterpret_cast<uint32_t*>(meta + g * 4) = pack_f16x2(e.s, e.z);
+    }
+  }
+}
+
+// Values a receiver reconstructs from an Enc8 (uses the scale as stored on the wire).
+template <int P, typename WT>
+QFC_DEV void decode8(const Enc8& e, int meta_fp32, float (&d)[8]) {
+  if constexpr (P == 16) {
+    if constexpr (sizeof(WT) == 2) {
+      const uint32_t w[4] = {e.a.x, e.a.y, e.a.z, e.a.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if constexpr (std::is_same<WT, __nv_bfloat16>::value) unpack_bf16x2(w[i], d[2 * i], d[2 * i + 1]);
+        else unpack_f16x2(w[i], d[2 * i], d[2 * i + 1]);
+      }
+    } else {
+      d[0] = __uint_as_float(e.a.x); d[1] = __uint_as_float(e.a.y);
+      d[2] = __uint_as_float(e.a.z); d[3] = __uint_as_float(e.a.w);
+      d[4] = __uint_as_float(e.b.x); d[5] = __uint_as_float(e.b.y);
+      d[6] = __uint_as_float(e.b.z); d[7] = __uint_as_float(e.b.w);
+    }
+  } else {
+    uint32_t c[8];
+    if constexpr (P == 8) u2_to_codes8(make_uint2(e.a.x, e.a.y), c);
+    else int4_to_codes8(e.a.x, c);
+    const float ss = meta_fp32 ? e.s : __half2float(__float2half_rn(e.s));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = dq(c[i], e.z, ss);
+  }
+}
+
+// Read one lane's 8 elements back from a slot in local memory (L2, bypassing L1: the
+// bytes were written by another GPU).
+template <int P, typename WT>
+QFC_DEV void load8(const char* slot, const char* meta, int64_t loc, int gs, int meta_fp32, float (&d)[8]) {
+  if constexpr (P == 16) {
+    Vec8IO<WT>::load_cg(reinterpret_cast<const WT*>(slot) + loc, d);
+  } else {
+    const int64_t g = loc / gs;
+    float s, z;
+    if (meta_fp32) {
+      const float2 m = __ldcg(reinterpret_cast<const float2*>(meta + g * 8));
+      s = m.x;
+      z = m.y;
+    } else {
+      const uint32_t m = __ldcg(reinterpret_cast<const unsigned int*>(meta + g * 4));
+      unpack_f16x2(m, s, z);
+    }
+    uint32_t c[8];
+    if constexpr (P == 8) u2_to_codes8(__ldcg(reinterpret_cast<const uint2*>(slot + loc)), c);
+    else int4_to_codes8(__ldcg(reinterpret_cast<const unsigned int*>(slot + (loc >> 1))), c);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = dq(c[i], z, s);
+  }
+}
+
+// Threads 0..W-1 each wait for one source's flag; returns false (for the whole CTA)
+// if any wait ran out.  skip_self: the own flag is not waited for.
+QFC_DEV bool wait_sources(const ARParams& p, char* my, int phase, int b, int rank, int W, uint32_t e,
+                          bool skip_self, int* s_abort) {
+  if ((int)threadIdx.x < W && !(skip_self && (int)threadIdx.x == rank)) {
+    uint32_t seen = 0;
+    const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+    if (!wait_flag_geq(flag_at(my, phase, b, threadIdx.x), e, deadline, seen)) {
+      report_timeout(p.status, phase, b, threadIdx.x, e, seen);
+      *s_abort = 1;
+    }
+  }
+  __syncthreads();
+  return *s_abort == 0;
+}
+
+template <typename InT, typename OutT, int P1, int P2>
+__global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ ARParams p) {
+  const int rank = gridDim.y > 1 ? (int)blockIdx.y : p.rank;
+  const int W = p.world;
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+  const int lpg = p.gs >> 3;
+  const bool leader = (lane & (lpg - 1)) == 0;
+  const InT* in = static_cast<const InT*>(p.in[rank]);
+  OutT* out = static_cast<OutT*>(p.out[rank]);
+  char* my = p.base[rank];
+  uint32_t* ep = p.epochs[rank] + ALG_TWO_SHOT * kMaxBlocks + b;
+  __shared__ uint32_t s_e;
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) {
+    s_e = *ep + 1u;
+    s_abort = 0;
+  }
+  __syncthreads();
+  const uint32_t e = s_e;
+  const int64_t C = p.chunk;
+  const int64_t units = C >> 8;
+  const int64_t ustride = (int64_t)gridDim.x * wpb;
+  const int64_t u0 = (int64_t)b * wpb + warp;
+
+  // Phase 1: quantize every chunk's units of this block, push to the chunk's owner.
+  for (int64_t u = u0; u < units; u += ustride) {
+    const int64_t loc = (u << 8) + lane * 8;
+#pragma unroll 1
+    for (int jj = 1; jj <= W; ++jj) {
+      const int j = (rank + jj) % W;  // peers staggered, own chunk last
+      if (j == rank && !p.quantize_local) continue;
+      float v[8];
+      load8_guard(in, (int64_t)j * C + loc, p.n, v);
+      const Enc8 en = encode8<P1, InT>(v, lpg, p.sym);
+      char* slot = p.base[j] + p.rs_off + (int64_t)rank * p.slot1;
+      store8<P1, InT>(slot, slot + p.pay1, loc, en, leader, p.gs, p.meta_fp32);
+    }
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < W) st_release_sys(flag_at(p.base[threadIdx.x], PH_RS, b, rank), e);
+  if (!wait_sources(p, my, PH_RS, b, rank, W, e, false, &s_abort)) return;
+
+  // Phase 2: reduce the own chunk, requantize, push to every peer, write own output.
+  for (int64_t u = u0; u < units; u += ustride) {
+    const int64_t loc = (u << 8) + lane * 8;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll 1
+    for (int s = 0; s < W; ++s) {
+      float d[8];
+      if (s == rank && !p.quantize_local) {
+        load8_guard(in, (int64_t)rank * C + loc, p.n, d);
+      } else {
+        const char* slot = my + p.rs_off + (int64_t)s * p.slot1;
+        load8<P1, InT>(slot, slot + p.pay1, loc, p.gs, p.meta_fp32, d);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], d[i]);
+    }
+    const Enc8 en = encode8<P2, InT>(acc, lpg, p.sym);
+#pragma unroll 1
+    for (int jj = 1; jj < W; ++jj) {
+      const int j = (rank + jj) % W;
+      char* slot = p.base[j] + p.ag_off + (int64_t)rank * p.slot2;
+      store8<P2, InT>(slot, slot + p.pay2, loc, en, leader, p.gs, p.meta_fp32);
+    }
+    float o[8];
+    decode8<P2, InT>(en, p.meta_fp32, o);
+    store8_guard(out, (int64_t)rank * C + loc, p.n, o);
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < W && (int)threadIdx.x != rank)
+    st_release_sys(flag_at(p.base[threadIdx.x], PH_AG, b, rank), e);
+  if (!wait_sources(p, my, PH_AG, b, rank, W, e, true, &s_abort)) return;
+
+  // Phase 3: dequantize the gathered chunks of the other ranks.
+  for (int64_t u = u0; u < units; u += ustride) {
+    const int64_t loc = (u << 8) + lane * 8;
+#pragma unroll 1
+    for (int jj = 1; jj < W; ++jj) {
+      const int j = (rank + jj) % W;
+      const char* slot = my + p.ag_off + (int64_t)j * p.slot2;
+      float d[8];
+      load8<P2, InT>(slot, slot + p.pay2, loc, p.gs, p.meta_fp32, d);
+      store8_guard(out, (int64_t)j * C + loc, p.n, d);
+    }
+  }
+  if (threadIdx.x == 0) *ep = e;
+}
+
+template <typename InT, typename OutT, int P>
+__global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ ARParams p) {
+  const int rank = gridDim.y > 1 ? (int)blockIdx.y : p.rank;
+  const int W = p.world;
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+  const int lpg = p.gs >> 3;
+  const bool leader = (lane & (lpg - 1)) == 0;
+  const InT* in = static_cast<const InT*>(p.in[rank]);
+  OutT* out = static_cast<OutT*>(p.out[rank]);
+  char* my = p.base[rank];
+  uint32_t* ep = p.epochs[rank] + ALG_ONE_SHOT * kMaxBlocks + b;
+  __shared__ uint32_t s_e;
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) {
+    s_e = *ep + 1u;
+    s_abort = 0;
+  }
+  __syncthreads();
+  const uint32_t e = s_e;
+  // Double-buffered by epoch parity: a peer may start call k+1 while this rank still
+  // reads call k's slots.
+  const int64_t region = p.os_off + (int64_t)(e & 1u) * p.os_bytes;
+  const int64_t units = p.chunk >> 8;
+  const int64_t ustride = (int64_t)gridDim.x * wpb;
+  const int64_t u0 = (int64_t)b * wpb + warp;
+
+  for (int64_t u = u0; u < units; u += ustride) {
+    const int64_t loc = (u << 8) + lane * 8;
+    float v[8];
+    load8_guard(in, loc, p.n, v);
+    const Enc8 en = encode8<P, InT>(v, lpg, p.sym);
+#pragma unroll 1
+    for (int jj = 1; jj < W; ++jj) {
+      const int j = (rank + jj) % W;
+      char* slot = p.base[j] + region + (int64_t)rank * p.slot1;
+      store8<P, InT>(slot, slot + p.pay1, loc, en, leader, p.gs, p.meta_fp32);
+    }
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < W && (int)threadIdx.x != rank)
+    st_release_sys(flag_at(p.base[threadIdx.x], PH_OS, b, rank), e);
+  if (!wait_sources(p, my, PH_OS, b, rank, W, e, true, &s_abort)) return;
+
+  for (int64_t u = u0; u < units; u += ustride) {
+    const int64_t loc = (u << 8) + lane * 8;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll 1
+    for (int s = 0; s < W; ++s) {
+      float d[8];
+      if (s == rank) {
+        float v[8];
+        load8_guard(in, loc, p.n, v);
+        if (p.quantize_local) {
+          const Enc8 en = encode8<P, InT>(v, lpg, p.sym);
+          decode8<P, InT>(en, p.meta_fp32, d);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) d[i] = v[i];
+        }
+      } else {
+        const char* slot = my + region + (int64_t)s * p.slot1;
+        load8<P, InT>(slot, slot + p.pay1, loc, p.gs, p.meta_fp32, d);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], d[i]);
+    }
+    store8_guard(out, loc, p.n, acc);
+  }
+  if (threadIdx.x == 0) *ep = e;
+}
+
+// ---------------------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------------------
+struct Plan {
+  int p1, p2;
+  int64_t chunk, slot1, slot2, pay1, pay2;
+  int64_t need_rs, need_ag, need_os;
+};
+
+int64_t payload_bytes(int64_t elems, int P, int in_elem) {
+  if (P == 16) return elems * in_elem;
+  return P == 8 ? elems : elems / 2;
+}
+int64_t meta_bytes(int64_t elems, int P, int gs, bool fp32) {
+  if (P == 16) return 0;
+  return (elems / gs) * (fp32 ? 8 : 4);
+}
+
+void phase_bits(int bits, int& p1, int& p2) {
+  switch (bits) {
+    case 16: p1 = 16; p2 = 16; break;
+    case 8: p1 = 8; p2 = 8; break;
+    case 6: p1 = 4; p2 = 8; break;
+    case 4: p1 = 4; p2 = 4; break;
+    default: TORCH_CHECK(false, "quant_all_reduce: bits must be 16, 8, 6 or 4; got ", bits);
+  }
+}
+
+Plan make_plan(int64_t n, int W, int bits, int gs, bool fp32, int in_elem, bool one_shot) {
+  Plan pl;
+  phase_bits(bits, pl.p1, pl.p2);
+  if (one_shot) {
+    // A single quantization step; INT6 uses its wider (INT8) half.
+    const int P = (bits == 6) ? 8 : pl.p1;
+    pl.p1 = pl.p2 = P;
+    pl.chunk = align_up(std::max<int64_t>(n, 1), 256);
+    pl.pay1 = align_up(payload_bytes(pl.chunk, P, in_elem), 256);
+    pl.slot1 = pl.pay1 + align_up(meta_bytes(pl.chunk, P, gs, fp32), 256);
+    pl.pay2 = pl.pay1;
+    pl.slot2 = pl.slot1;
+    pl.need_rs = pl.need_ag = 0;
+    pl.need_os = (int64_t)W * pl.slot1;
+  } else {
+    pl.chunk = align_up((std::max<int64_t>(n, 1) + W - 1) / W, 256);
+    pl.pay1 = align_up(payload_bytes(pl.chunk, pl.p1, in_elem), 256);
+    pl.slot1 = pl.pay1 + align_up(meta_bytes(pl.chunk, pl.p1, gs, fp32), 256);
+    pl.pay2 = align_up(payload_bytes(pl.chunk, pl.p2, in_elem), 256);
+    pl.slot2 = pl.pay2 + align_up(meta_bytes(pl.chunk, pl.p2, gs, fp32), 256);
+    pl.need_rs = (int64_t)W * pl.slot1;
+    pl.need_ag = (int64_t)W * pl.slot2;
+    pl.need_os = 0;
+  }
+  return pl;
+}
+
+int num_sms(int dev) {
+  static int cached[64] = {0};
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  int v = 0;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < 64) cached[dev] = v;
+  return v;
+}
+
+template <typename Kern>
+void launch_ar(Kern kern, const ARParams& prm, int64_t units, int W_emul, int dev, cudaStream_t st) {
+  const int sms = num_sms(dev);
+  int wpb = (int)std::min<int64_t>(16, std::max<int64_t>(2, (units + sms - 1) / sms));
+  const int threads = wpb * 32;
+  int occ = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, 0);
+  if (occ < 1) occ = 1;
+  int64_t cap = (int64_t)occ * sms / std::max(1, W_emul);
+  cap = std::min<int64_t>(cap, std::min<int64_t>(sms, kMaxBlocks));
+  TORCH_CHECK(cap >= 1, "quant_all_reduce: no co-resident CTA budget (emulated world too large)");
+  const int64_t G = std::max<int64_t>(1, std::min<int64_t>((units + wpb - 1) / wpb, cap));
+  dim3 grid((unsigned)G, (unsigned)std::max(1, W_emul));
+  kern<<<grid, threads, 0, st>>>(prm);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <typename InT, typename OutT>
+void dispatch_bits(const ARParams& prm, const Plan& pl, bool one_shot, int64_t units, int W_emul, int dev,
+                   cudaStream_t st) {
+  if (one_shot) {
+    switch (pl.p1) {
+      case 16: launch_ar(one_shot_kernel<InT, OutT, 16>, prm, units, W_emul, dev, st); break;
+      case 8: launch_ar(one_shot_kernel<InT, OutT, 8>, prm, units, W_emul, dev, st); break;
+      default: launch_ar(one_shot_kernel<InT, OutT, 4>, prm, units, W_emul, dev, st); break;
+    }
+    return;
+  }
+  if (pl.p1 == 16) launch_ar(two_shot_kernel<InT, OutT, 16, 16>, prm, units, W_emul, dev, st);
+  else if (pl.p1 == 8) launch_ar(two_shot_kernel<InT, OutT, 8, 8>, prm, units, W_emul, dev, st);
+  else if (pl.p2 == 8) launch_ar(two_shot_kernel<InT, OutT, 4, 8>, prm, units, W_emul, dev, st);
+  else launch_ar(two_shot_kernel<InT, OutT, 4, 4>, prm, units, W_emul, dev, st);
+}
+
+}  // namespace
+
+using WsPtr = std::shared_ptr<Workspace>;
+
+// Region sizes a call needs: (chunk, need_rs, need_ag, need_os) for the given algorithm.
+std::vector<int64_t> ar_plan(int64_t n, int64_t world, int64_t bits, int64_t gs, bool scale_fp32,
+                             int64_t in_elem_size, bool one_shot) {
+  const Plan pl = make_plan(n, (int)world, (int)bits, (int)gs, scale_fp32, (int)in_elem_size, one_shot);
+  return {pl.chunk, pl.need_rs, pl.need_ag, pl.need_os};
+}
+
+// wss: one workspace (normal, this rank) or W workspaces (single-GPU emulation, one per
+// emulated rank, all on the current device).  ins / outs: one tensor per entry of wss.
+void quant_all_reduce(const std::vector<WsPtr>& wss, const std::vector<at::Tensor>& ins,
+                      const std::vector<at::Tensor>& outs, int64_t bits, int64_t gs, bool sym,
+                      bool scale_fp32, bool one_shot, bool quantize_local, double timeout_ms) {
+  TORCH_CHECK(!wss.empty() && wss.size() == ins.size() && ins.size() == outs.size(),
+              "quant_all_reduce: need one input and one output per workspace");
+  const int W = (int)wss[0]->world();
+  const bool emulate = wss.size() > 1;
+  TORCH_CHECK(!emulate || (int)wss.size() == W, "quant_all_reduce: emulation needs W workspaces");
+  TORCH_CHECK(gs >= 8 && gs <= 256 && (gs & (gs - 1)) == 0,
+              "quant_all_reduce: fused kernel supports power-of-two group sizes 8..256, got ", gs);
+  const int64_t n = ins[0].numel();
+  const auto in_dt = ins[0].scalar_type();
+  const auto out_dt = outs[0].scalar_type();
+  for (size_t i = 0; i < ins.size(); ++i) {
+    TORCH_CHECK(ins[i].is_cuda() && outs[i].is_cuda(), "quant_all_reduce: CUDA tensors required");
+    TORCH_CHECK(ins[i].numel() == n && outs[i].numel() == n, "quant_all_reduce: size mismatch");
+    TORCH_CHECK(ins[i].is_contiguous() && outs[i].is_contiguous(), "quant_all_reduce: contiguous tensors required");
+    TORCH_CHECK(ins[i].scalar_type() == in_dt && outs[i].scalar_type() == out_dt, "quant_all_reduce: dtype mismatch");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(ins[i].data_ptr()) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(outs[i].data_ptr()) % 16 == 0,
+                "quant_all_reduce: tensors must be 16-byte aligned");
+    TORCH_CHECK(wss[i]->peers_ready(), "quant_all_reduce: workspace peers not mapped");
+  }
+  if (n == 0) return;
+  c10::cuda::CUDAGuard guard(ins[0].device());
+  const int dev = ins[0].get_device();
+  const int in_elem = (int)ins[0].element_size();
+  const Plan pl = make_plan(n, W, (int)bits, (int)gs, scale_fp32, in_elem, one_shot);
+  const Workspace& w0 = *wss[0];
+  TORCH_CHECK(pl.need_rs <= w0.rs_bytes() && pl.need_ag <= w0.ag_bytes() && pl.need_os <= w0.os_bytes(),
+              "quant_all_reduce: workspace too small for this message (grow it first)");
+  ARParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  for (int r = 0; r < W; ++r) {
+    if (emulate) {
+      prm.in[r] = ins[r].data_ptr();
+      prm.out[r] = outs[r].data_ptr();
+      prm.base[r] = wss[r]->base();
+      prm.epochs[r] = wss[r]->epochs();
+    } else {
+      prm.base[r] = w0.peer_base(r);
+    }
+  }
+  if (!emulate) {
+    const int rk = (int)w0.rank();
+    prm.in[rk] = ins[0].data_ptr();
+    prm.out[rk] = outs[0].data_ptr();
+    prm.epochs[rk] = w0.epochs();
+  }
+  prm.status = w0.status_dev();
+  prm.n = n;
+  prm.chunk = pl.chunk;
+  prm.rs_off = w0.rs_off();
+  prm.ag_off = w0.ag_off();
+  prm.os_off = w0.os_off();
+  prm.os_bytes = w0.os_bytes();
+  prm.slot1 = pl.slot1;
+  prm.slot2 = pl.slot2;
+  prm.pay1 = pl.pay1;
+  prm.pay2 = pl.pay2;
+  prm.timeout_ns = (uint64_t)(timeout_ms * 1e6);
+  prm.world = W;
+  prm.rank = emulate ? 0 : (int)w0.rank();
+  prm.gs = (int)gs;
+  prm.meta_fp32 = scale_fp32 ? 1 : 0;
+  prm.sym = sym ? 1 : 0;
+  prm.quantize_local = quantize_local ? 1 : 0;
+  const int64_t units = pl.chunk >> 8;
+  const int W_emul = emulate ? W : 1;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  auto go = [&](auto in_tag, auto out_tag) {
+    dispatch_bits<decltype(in_tag), decltype(out_tag)>(prm, pl, one_shot, units, W_emul, dev, st);
+  };
+  if (in_dt == at::kBFloat16 && out_dt == at::kBFloat16) go(__nv_bfloat16(), __nv_bfloat16());
+  else if (in_dt == at::kBFloat16 && out_dt == at::kHalf) go(__nv_bfloat16(), __half());
+  else if (in_dt == at::kHalf && out_dt == at::kHalf) go(__half(), __half());
+  else if (in_dt == at::kFloat && out_dt == at::kFloat) go(float(), float());
+  else if (in_dt == at::kFloat && out_dt == at::kHalf) go(float(), __half());
+  else TORCH_CHECK(false, "quant_all_reduce: unsupported (input, output) dtype pair ", in_dt, ", ", out_dt);
+}
+
+}  // namespace qfc

@@ -1,0 +1,71 @@
+// Python bindings of the native extension (quantized_flash_communication_b200._C).
+#include <pybind11/stl.h>
+#include <torch/extension.h>
+
+#include <memory>
+
+#include "workspace.h"
+
+namespace qfc {
+// quant_kernels.cu
+std::vector<at::Tensor> quantize_cuda(const at::Tensor& x, int64_t bits, int64_t group_size, bool sym,
+                                      bool scale_fp32);
+at::Tensor dequantize_cuda(const at::Tensor& q, const at::Tensor& s, const at::Tensor& z, int64_t group_size,
+                           at::ScalarType out_dtype);
+at::Tensor pack_int4_cuda(const at::Tensor& codes);
+at::Tensor unpack_int4_cuda(const at::Tensor& words, int64_t numel);
+// quant_cpu.cpp
+std::vector<at::Tensor> quantize_cpu(const at::Tensor& x, int64_t bits, int64_t group_size, bool sym,
+                                     bool scale_fp32);
+at::Tensor dequantize_cpu(const at::Tensor& q, const at::Tensor& s, const at::Tensor& z, int64_t group_size,
+                          at::ScalarType out_dtype);
+at::Tensor pack_int4_cpu(const at::Tensor& codes);
+at::Tensor unpack_int4_cpu(const at::Tensor& words, int64_t numel);
+// allreduce.cu
+std::vector<int64_t> ar_plan(int64_t n, int64_t world, int64_t bits, int64_t gs, bool scale_fp32,
+                             int64_t in_elem_size, bool one_shot);
+void quant_all_reduce(const std::vector<std::shared_ptr<Workspace>>& wss, const std::vector<at::Tensor>& ins,
+                      const std::vector<at::Tensor>& outs, int64_t bits, int64_t gs, bool sym, bool scale_fp32,
+                      bool one_shot, bool quantize_local, double timeout_ms);
+}  // namespace qfc
+
+namespace py = pybind11;
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "B200-native kernels for quantized tensor-parallel communication";
+
+  m.def("quantize", &qfc::quantize_cuda, "blockwise quantize (CUDA)", py::arg("x"), py::arg("bits"),
+        py::arg("group_size"), py::arg("sym"), py::arg("scale_fp32"));
+  m.def("dequantize", &qfc::dequantize_cuda, "blockwise dequantize (CUDA)", py::arg("q"), py::arg("s"),
+        py::arg("z"), py::arg("group_size"), py::arg("out_dtype"));
+  m.def("pack_int4", &qfc::pack_int4_cuda, "pack 4-bit codes into int32 words (CUDA)");
+  m.def("unpack_int4", &qfc::unpack_int4_cuda, "unpack int32 words into fp16 codes (CUDA)");
+
+  m.def("quantize_cpu", &qfc::quantize_cpu, "blockwise quantize (C++ CPU oracle)");
+  m.def("dequantize_cpu", &qfc::dequantize_cpu, "blockwise dequantize (C++ CPU oracle)");
+  m.def("pack_int4_cpu", &qfc::pack_int4_cpu, "pack 4-bit codes (C++ CPU oracle)");
+  m.def("unpack_int4_cpu", &qfc::unpack_int4_cpu, "unpack 4-bit codes to uint8 (C++ CPU oracle)");
+
+  py::class_<qfc::Workspace, std::shared_ptr<qfc::Workspace>>(m, "Workspace")
+      .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, int64_t>(), py::arg("device"),
+           py::arg("rank"), py::arg("world"), py::arg("rs_bytes"), py::arg("ag_bytes"), py::arg("os_bytes"))
+      .def("ipc_handle", [](const qfc::Workspace& w) { return py::bytes(w.ipc_handle()); })
+      .def("open_peers", &qfc::Workspace::open_peers)
+      .def("set_peer_ptrs", &qfc::Workspace::set_peer_ptrs)
+      .def("status", &qfc::Workspace::status)
+      .def("clear_status", &qfc::Workspace::clear_status)
+      .def_property_readonly("local_ptr", &qfc::Workspace::local_ptr)
+      .def_property_readonly("device", &qfc::Workspace::device)
+      .def_property_readonly("rank", &qfc::Workspace::rank)
+      .def_property_readonly("world", &qfc::Workspace::world)
+      .def_property_readonly("rs_bytes", &qfc::Workspace::rs_bytes)
+      .def_property_readonly("ag_bytes", &qfc::Workspace::ag_bytes)
+      .def_property_readonly("os_bytes", &qfc::Workspace::os_bytes)
+      .def_property_readonly("peers_ready", &qfc::Workspace::peers_ready);
+
+  m.def("ar_plan", &qfc::ar_plan, "region sizes a quantized all-reduce call needs");
+  m.def("quant_all_reduce", &qfc::quant_all_reduce, "fused quantized all-reduce over peer memory",
+        py::arg("workspaces"), py::arg("ins"), py::arg("outs"), py::arg("bits"), py::arg("group_size"),
+        py::arg("sym"), py::arg("scale_fp32"), py::arg("one_shot"), py::arg("quantize_local"),
+        py::arg("timeout_ms"));
+}

@@ -1,0 +1,158 @@
+"""Quantized all-reduce over peer memory: the fused single-kernel path.
+
+:class:`QuantAllReduce` owns a :class:`SymmetricWorkspace` for one process group and
+launches the fused kernel of ``csrc/allreduce.cu`` (two-shot for large messages, one-shot
+for small ones).  It never calls NCCL on the data path.
+
+Reference capability: ``flash_all_reduce`` (communication.py:7-97); knobs ``bits``
+(16 / 8 / 6 / 4), ``group_size`` and ``quant_type`` ("asym" / "sym") keep their meaning.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+from .._ext import ext
+from .symm_mem import EmulatedWorkspaces, SymmetricWorkspace, default_timeout_ms
+
+__all__ = ["QuantAllReduce", "EmulatedQuantAllReduce", "ONE_SHOT_MAX_BYTES"]
+
+# Messages up to this many input bytes use the one-shot algorithm under algo="auto".
+ONE_SHOT_MAX_BYTES = 512 * 1024
+
+_OUT_PAIRS = {
+    (torch.bfloat16, torch.bfloat16), (torch.bfloat16, torch.float16), (torch.float16, torch.float16),
+    (torch.float32, torch.float32), (torch.float32, torch.float16),
+}
+
+
+def _pick_one_shot(algo: str, nbytes: int, one_shot_max: int) -> bool:
+    if algo == "one_shot":
+        return True
+    if algo == "two_shot":
+        return False
+    if algo != "auto":
+        raise ValueError(f"algo must be 'auto', 'one_shot' or 'two_shot', got {algo!r}")
+    return nbytes <= one_shot_max
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+class _Base:
+    def __init__(self, bits: int, group_size: int, quant_type: str, scale_dtype: torch.dtype, algo: str,
+                 one_shot_max_bytes: int, quantize_local: bool, timeout_ms: Optional[float]):
+        if quant_type not in ("asym", "sym"):
+            raise ValueError("quant_type must be 'asym' or 'sym'")
+        if group_size < 8 or group_size > 256 or group_size & (group_size - 1):
+            raise ValueError("the fused all-reduce takes power-of-two group sizes 8..256")
+        self.bits = bits
+        self.group_size = group_size
+        self.quant_type = quant_type
+        self.scale_dtype = scale_dtype
+        self.algo = algo
+        self.one_shot_max_bytes = one_shot_max_bytes
+        self.quantize_local = quantize_local
+        self.timeout_ms = default_timeout_ms() if timeout_ms is None else timeout_ms
+
+    def _plan(self, n: int, W: int, elem: int, bits: int, gs: int, fp32: bool, one_shot: bool):
+        _, need_rs, need_ag, need_os = ext().ar_plan(n, W, bits, gs, fp32, elem, one_shot)
+        return need_rs, need_ag, need_os
+
+
+class QuantAllReduce(_Base):
+    """Fused quantized all-reduce for one process group (one rank per GPU).
+
+    ``ar(x)`` returns the all-reduced tensor (``out`` may alias ``x``).  Every rank must
+    call it with the same shape, dtype and settings, in the same order.
+    """
+
+    def __init__(self, group: Optional[dist.ProcessGroup] = None, device=None, bits: int = 8,
+                 group_size: int = 128, quant_type: str = "asym", scale_dtype: torch.dtype = torch.float16,
+                 algo: str = "auto", one_shot_max_bytes: int = ONE_SHOT_MAX_BYTES,
+                 quantize_local: bool = True, timeout_ms: Optional[float] = None,
+                 reserve_elems: int = 0, reserve_dtype: torch.dtype = torch.bfloat16):
+        super().__init__(bits, group_size, quant_type, scale_dtype, algo, one_shot_max_bytes, quantize_local,
+                         timeout_ms)
+        self.group = group
+        self.ws = SymmetricWorkspace(group, device)
+        self.world = self.ws.world
+        self.rank = self.ws.rank
+        if reserve_elems:
+            self.reserve(reserve_elems, reserve_dtype)
+
+    def reserve(self, max_elems: int, dtype: torch.dtype = torch.bfloat16, bits_options: Sequence[int] = (16, 8, 6, 4)):
+        """Size the workspace for messages up to ``max_elems`` (call before graph capture)."""
+        elem = torch.empty((), dtype=dtype).element_size()
+        rs = ag = os_ = 0
+        for b in bits_options:
+            for one in (False, True):
+                if one and max_elems * elem > self.one_shot_max_bytes and self.algo != "one_shot":
+                    continue
+                r, a, o = self._plan(max_elems, self.world, elem, b, self.group_size,
+                                     self.scale_dtype == torch.float32, one)
+                rs, ag, os_ = max(rs, r), max(ag, a), max(os_, o)
+        self.ws.ensure(rs, ag, os_)
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                 bits: Optional[int] = None, group_size: Optional[int] = None, quant_type: Optional[str] = None,
+                 algo: Optional[str] = None) -> torch.Tensor:
+        bits = self.bits if bits is None else bits
+        gs = self.group_size if group_size is None else group_size
+        qt = self.quant_type if quant_type is None else quant_type
+        algo = self.algo if algo is None else algo
+        x = _aligned(x)
+        if out is None:
+            out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+        if (x.dtype, out.dtype) not in _OUT_PAIRS:
+            raise TypeError(f"unsupported (input, output) dtypes {x.dtype}, {out.dtype}")
+        one = _pick_one_shot(algo, x.numel() * x.element_size(), self.one_shot_max_bytes)
+        fp32 = self.scale_dtype == torch.float32
+        self.ws.ensure(*self._plan(x.numel(), self.world, x.element_size(), bits, gs, fp32, one))
+        ext().quant_all_reduce([self.ws.native], [x], [out], bits, gs, qt == "sym", fp32, one,
+                               self.quantize_local, self.timeout_ms)
+        return out
+
+    def check(self, synchronize: bool = True):
+        self.ws.check(synchronize)
+
+
+class EmulatedQuantAllReduce(_Base):
+    """W ranks of the fused all-reduce inside single launches on one GPU (testing aid)."""
+
+    def __init__(self, world: int, device=None, bits: int = 8, group_size: int = 128, quant_type: str = "asym",
+                 scale_dtype: torch.dtype = torch.float16, algo: str = "auto",
+                 one_shot_max_bytes: int = ONE_SHOT_MAX_BYTES, quantize_local: bool = True,
+                 timeout_ms: Optional[float] = None):
+        super().__init__(bits, group_size, quant_type, scale_dtype, algo, one_shot_max_bytes, quantize_local,
+                         timeout_ms)
+        self.ws = EmulatedWorkspaces(world, device)
+        self.world = world
+
+    def __call__(self, xs: List[torch.Tensor], outs: Optional[List[torch.Tensor]] = None,
+                 out_dtype: Optional[torch.dtype] = None, bits: Optional[int] = None,
+                 group_size: Optional[int] = None, quant_type: Optional[str] = None,
+                 algo: Optional[str] = None) -> List[torch.Tensor]:
+        assert len(xs) == self.world
+        bits = self.bits if bits is None else bits
+        gs = self.group_size if group_size is None else group_size
+        qt = self.quant_type if quant_type is None else quant_type
+        algo = self.algo if algo is None else algo
+        xs = [_aligned(x) for x in xs]
+        if outs is None:
+            outs = [torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device) for x in xs]
+        one = _pick_one_shot(algo, xs[0].numel() * xs[0].element_size(), self.one_shot_max_bytes)
+        fp32 = self.scale_dtype == torch.float32
+        self.ws.ensure(*self._plan(xs[0].numel(), self.world, xs[0].element_size(), bits, gs, fp32, one))
+        ext().quant_all_reduce(self.ws.all, xs, outs, bits, gs, qt == "sym", fp32, one, self.quantize_local,
+                               self.timeout_ms)
+        return outs
+
+    def check(self, synchronize: bool = True):
+        self.ws.check(synchronize)

@@ -1,0 +1,137 @@
+"""Fused quantized all-reduce kernel on ONE GPU, with W ranks emulated in one launch.
+
+Each emulated rank has its own workspace; block row y of the launch plays rank y and
+stores into the other ranks' buffers, so the flag protocol, slot layout and numerics of
+the multi-GPU kernel run unchanged.  Results must equal the oracle bit for bit and be
+identical on every rank.
+"""
+import pytest
+import torch
+
+from quantized_flash_communication_b200 import quantization as spec
+from quantized_flash_communication_b200._ext import ext
+from quantized_flash_communication_b200.parallel import EmulatedQuantAllReduce
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(W, shape, dtype, device, seed=0):
+    xs = []
+    for r in range(W):
+        g = torch.Generator(device="cpu").manual_seed(seed + r)
+        x = torch.randn(*shape, generator=g)
+        x.view(-1)[::1000] *= 50  # 0.1% outliers
+        xs.append(x.to(dtype).to(device))
+    return xs
+
+
+CASES = [
+    # (W, bits, gs, mode, shape, algo)
+    (2, 8, 128, "asym", (8, 4096), "two_shot"),
+    (8, 8, 128, "asym", (128, 4096), "two_shot"),
+    (8, 6, 128, "asym", (16, 8192), "two_shot"),
+    (8, 4, 128, "sym", (16, 4096), "two_shot"),
+    (4, 8, 32, "sym", (3, 1000), "two_shot"),
+    (4, 4, 64, "asym", (1, 4096), "two_shot"),
+    (8, 16, 128, "asym", (1024, 4096), "two_shot"),
+    (1, 8, 128, "asym", (5, 4096), "two_shot"),
+    (2, 8, 128, "asym", (1, 4096), "one_shot"),
+    (8, 8, 128, "asym", (64, 4096), "one_shot"),
+    (8, 4, 128, "sym", (7, 999), "one_shot"),
+    (8, 6, 256, "asym", (4, 4096), "one_shot"),
+    (4, 16, 128, "asym", (16, 4096), "one_shot"),
+]
+
+
+@pytest.mark.parametrize("W,bits,gs,mode,shape,algo", CASES)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_emulated_matches_oracle(cuda_device, W, bits, gs, mode, shape, algo, dtype):
+    ar = EmulatedQuantAllReduce(W, cuda_device, bits=bits, group_size=gs, quant_type=mode, algo=algo,
+                                timeout_ms=5000)
+    xs = _inputs(W, shape, dtype, cuda_device, seed=W * 100 + bits)
+    for it in range(3):  # repeated calls exercise epochs and slot reuse
+        outs = ar(xs)
+        ar.check()
+        cpu = [x.cpu() for x in xs]
+        if algo == "two_shot":
+            ref = spec.two_step_all_reduce_ref(cpu, bits, gs, mode, torch.float16, dtype)
+        else:
+            ref = spec.one_shot_all_reduce_ref(cpu, bits, gs, mode, torch.float16, dtype)
+        for r in range(W):
+            assert torch.equal(outs[r].cpu(), ref), (it, r)
+        xs = [x.roll(1) for x in xs]
+
+
+@pytest.mark.parametrize("scale_dtype", [torch.float32])
+def test_fp32_scales_and_fp16_output(cuda_device, scale_dtype):
+    W = 4
+    ar = EmulatedQuantAllReduce(W, cuda_device, bits=8, group_size=128, quant_type="sym", scale_dtype=scale_dtype,
+                                algo="two_shot")
+    xs = _inputs(W, (32, 4096), torch.bfloat16, cuda_device)
+    outs = ar(xs, out_dtype=torch.float16)
+    ar.check()
+    ref = spec.two_step_all_reduce_ref([x.cpu() for x in xs], 8, 128, "sym", scale_dtype, torch.float16)
+    for r in range(W):
+        assert torch.equal(outs[r].cpu(), ref)
+
+
+def test_exact_local_contribution(cuda_device):
+    W = 2
+    ar = EmulatedQuantAllReduce(W, cuda_device, bits=8, group_size=128, algo="two_shot", quantize_local=False)
+    xs = _inputs(W, (4, 4096), torch.float32, cuda_device)
+    outs = ar(xs)
+    ar.check()
+    exact = (xs[0] + xs[1]).cpu()
+    assert spec.rel_l2(outs[0].cpu(), exact) < 0.01
+    assert torch.equal(outs[0].cpu(), outs[1].cpu())
+
+
+def test_in_place(cuda_device):
+    W = 4
+    ar = EmulatedQuantAllReduce(W, cuda_device, bits=8, group_size=128, algo="two_shot")
+    xs = _inputs(W, (16, 4096), torch.bfloat16, cuda_device)
+    ref = spec.two_step_all_reduce_ref([x.cpu() for x in xs], 8, 128, "asym", torch.float16, torch.bfloat16)
+    ar(xs, outs=xs)
+    ar.check()
+    for r in range(W):
+        assert torch.equal(xs[r].cpu(), ref)
+
+
+def test_cuda_graph_replay(cuda_device):
+    W = 4
+    ar = EmulatedQuantAllReduce(W, cuda_device, bits=8, group_size=128, algo="auto")
+    xs = _inputs(W, (64, 4096), torch.bfloat16, cuda_device)
+    outs = [torch.empty_like(x) for x in xs]
+    ar(xs, outs)  # warm-up sizes the workspaces
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ar(xs, outs)
+    for it in range(4):
+        for x in xs:
+            x.copy_(torch.randn_like(x))
+        g.replay()
+        ar.check()
+        ref = spec.one_shot_all_reduce_ref([x.cpu() for x in xs], 8, 128, "asym", torch.float16, torch.bfloat16)
+        for r in range(W):
+            assert torch.equal(outs[r].cpu(), ref), it
+
+
+def test_timeout_reports_status_and_context_survives(cuda_device):
+    """Rank 0 of a 2-rank workspace whose peer never runs: every wait must expire."""
+    C = ext()
+    ws0 = C.Workspace(0, 0, 2, 1 << 22, 1 << 22, 1 << 22)
+    ws1 = C.Workspace(0, 1, 2, 1 << 22, 1 << 22, 1 << 22)  # "peer" memory nobody signals
+    ws0.set_peer_ptrs([ws0.local_ptr, ws1.local_ptr])
+    x = torch.randn(8, 4096, device=cuda_device, dtype=torch.bfloat16)
+    out = torch.empty_like(x)
+    C.quant_all_reduce([ws0], [x], [out], 8, 128, False, False, False, True, 50.0)
+    torch.cuda.synchronize()
+    code, phase, block, peer, want, seen = ws0.status()
+    assert code == 1 and phase == 0 and peer == 1 and want == 1 and seen == 0
+    ws0.clear_status()
+    assert ws0.status()[0] == 0
+    # the context is still usable
+    y = (x.float() * 2).sum()
+    torch.cuda.synchronize()
+    assert torch.isfinite(y)
