@@ -27,6 +27,19 @@ std::vector<int64_t> ar_plan(int64_t n, int64_t world, int64_t bits, int64_t gs,
 void quant_all_reduce(const std::vector<std::shared_ptr<Workspace>>& wss, const std::vector<at::Tensor>& ins,
                       const std::vector<at::Tensor>& outs, int64_t bits, int64_t gs, bool sym, bool scale_fp32,
                       bool one_shot, bool quantize_local, double timeout_ms);
+// gemm.cu
+at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& out, int64_t epi,
+                     const c10::optional<at::Tensor>& residual, double timeout_ms, int64_t max_ctas);
+int64_t gemm_status(bool clear);
+// layers.cu
+void rmsnorm_cuda(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& y,
+                  double eps);
+void rope_kv_cuda(at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& cos_sin,
+                  const c10::optional<at::Tensor>& k_cache, const c10::optional<at::Tensor>& v_cache,
+                  const c10::optional<at::Tensor>& slot_mapping, int64_t nq, int64_t nkv, int64_t hd);
+void silu_mul_cuda(const at::Tensor& gu, at::Tensor& out);
+void embedding_cuda(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t vocab_start);
+void argmax_cuda(const at::Tensor& logits, at::Tensor& best_val, at::Tensor& best_idx, int64_t idx_offset);
 }  // namespace qfc
 
 namespace py = pybind11;
@@ -62,6 +75,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("ag_bytes", &qfc::Workspace::ag_bytes)
       .def_property_readonly("os_bytes", &qfc::Workspace::os_bytes)
       .def_property_readonly("peers_ready", &qfc::Workspace::peers_ready);
+
+  m.def("gemm_bf16", &qfc::gemm_bf16, "tcgen05 GEMM a @ b^T with fused epilogue (0 store, 1 swiglu, 2 residual)",
+        py::arg("a"), py::arg("b"), py::arg("out") = py::none(), py::arg("epi") = 0,
+        py::arg("residual") = py::none(), py::arg("timeout_ms") = 10000.0, py::arg("max_ctas") = 0);
+  m.def("gemm_status", &qfc::gemm_status, py::arg("clear") = false);
+  m.def("rmsnorm", &qfc::rmsnorm_cuda, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("y"), py::arg("eps"));
+  m.def("rope_kv", &qfc::rope_kv_cuda, py::arg("qkv"), py::arg("pos"), py::arg("cos_sin"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("slot_mapping"), py::arg("nq"), py::arg("nkv"), py::arg("hd"));
+  m.def("silu_mul", &qfc::silu_mul_cuda);
+  m.def("embedding", &qfc::embedding_cuda);
+  m.def("argmax", &qfc::argmax_cuda);
 
   m.def("ar_plan", &qfc::ar_plan, "region sizes a quantized all-reduce call needs");
   m.def("quant_all_reduce", &qfc::quant_all_reduce, "fused quantized all-reduce over peer memory",

@@ -1,0 +1,453 @@
+// Persistent tcgen05 / TMEM GEMM for sm_100a:  D[M, N] = A[M, K] * B[N, K]^T  (bf16 in,
+// fp32 accumulate), the layout of nn.Linear (activations x weights^T).
+//
+// Replaces the cuBLAS GEMMs behind the reference's nn.Linear layers (model.py:32-35 and
+// the HF attention projections).  One CTA per SM, 6 warps:
+//   warp 0      TMA producer: 128x64 A tile + two 128x64 B half-tiles per stage, 128-byte
+//               swizzle, 4-stage ring of full / empty mbarriers (plain loads, no multicast);
+//   warp 1      TMEM allocator and MMA issuer: one elected thread issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) x4 per stage and
+//               commits each stage back to its empty barrier;
+//   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (each warp its 32-lane TMEM
+//               quarter), fused epilogue, 16-byte global stores.
+// The accumulator is double-buffered in TMEM (2 x 256 of the 512 columns), so the
+// epilogue of tile t overlaps the main loop of tile t+1.  Fused epilogues:
+//   EPI_STORE     bf16 D
+//   EPI_SWIGLU    B = [gate; up] (2I rows); each N tile holds 128 gate + 128 up columns
+//                 and writes silu(gate) * up (the reference's act_fn(gate) * up,
+//                 model.py:32-34) as bf16 [M, I]
+//   EPI_RESIDUAL  D = acc + R (bf16), for the residual stream when no all-reduce follows
+// Every mbarrier wait is bounded (%globaltimer); on expiry the CTA records an error code,
+// drains its in-flight copies and MMAs (bounded), frees TMEM and returns.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAException.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace qfc {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;        // 16 KiB
+constexpr int B_HALF_BYTES = 128 * BK * 2;  // 16 KiB
+constexpr int B_BYTES = 2 * B_HALF_BYTES;   // 32 KiB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int GROUP_M = 16;
+constexpr uint32_t IDESC = tc::idesc_f16(BM, BN, true);
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+enum Epi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_RESIDUAL = 2 };
+
+enum : int { GEMM_ERR_PRODUCER = 0x100, GEMM_ERR_MMA = 0x200, GEMM_ERR_EPI = 0x300 };
+
+struct GemmArgs {
+  int M, N, K;       // D[M, N]; for EPI_SWIGLU N is the output width I and B has 2I rows
+  int n_tiles;       // tiles along N
+  int n_tile_cols;   // output columns per N tile (256, or 128 for EPI_SWIGLU)
+  int b_second;      // row offset of the second 128-row half of a B tile
+  int b_first_step;  // rows of B advanced per N tile
+  __nv_bfloat16* D;
+  int ldd;
+  const __nv_bfloat16* R;
+  int ldr;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+QFC_DEV void tile_coords(int tile, int m_tiles, int n_tiles, int& mb, int& nb) {
+  const int group = GROUP_M * n_tiles;
+  const int g = tile / group;
+  const int first_m = g * GROUP_M;
+  const int gm = min(m_tiles - first_m, GROUP_M);
+  const int r = tile % group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+QFC_DEV void fail(const GemmArgs& a, volatile int* s_abort, int code) {
+  *s_abort = 1;
+  if (a.status) atomicCAS(a.status, 0, code);
+}
+
+QFC_DEV uint32_t pack_bf16(float lo, float hi) { return pack_bf16x2(lo, hi); }
+
+template <int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (args.M + BM - 1) / BM;
+  const int tiles = m_tiles * args.n_tiles;
+  const int kbs = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(tc::smem_u32(&full[s]), 1);
+      tc::mbar_init(tc::smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(tc::smem_u32(&tfull[b]), 1);
+      tc::mbar_init(tc::smem_u32(&tempty[b]), 128);
+    }
+    tc::mbar_init(tc::smem_u32(drain), 1);
+    *s_abort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::tma_prefetch_desc(&tmA);
+    tc::tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tc::smem_u32(tmem_holder), TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      int last_issue[STAGES];
+      for (int s = 0; s < STAGES; ++s) last_issue[s] = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, m_tiles, args.n_tiles, mb, nb);
+        const int yb = nb * args.b_first_step;
+        for (int kb = 0; kb < kbs; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!tc::mbar_wait(tc::smem_u32(&empty[s]), ph ^ 1, globaltimer_ns() + args.timeout_ns, s_abort)) {
+            fail(args, s_abort, GEMM_ERR_PRODUCER | 1);
+            ok = false;
+            break;
+          }
+          const uint32_t fb = tc::smem_u32(&full[s]);
+          tc::mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          tc::tma_load_2d(tc::smem_u32(sA + s * A_BYTES), &tmA, fb, kb * BK, mb * BM);
+          tc::tma_load_2d(tc::smem_u32(sB + s * B_BYTES), &tmB, fb, kb * BK, yb);
+          tc::tma_load_2d(tc::smem_u32(sB + s * B_BYTES + B_HALF_BYTES), &tmB, fb, kb * BK, yb + args.b_second);
+          last_issue[s] = it;
+        }
+      }
+      if (!ok || *s_abort) {
+        // Let every issued copy land before the CTA (and its shared memory) goes away.
+        for (int s = 0; s < STAGES; ++s) {
+          if (last_issue[s] < 0) continue;
+          const uint32_t ph = (last_issue[s] / STAGES) & 1;
+          int never = 0;
+          tc::mbar_wait(tc::smem_u32(&full[s]), ph, globaltimer_ns() + 50000000ull, &never);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int it = 0, t = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++t) {
+        const int buf = t & 1;
+        if (!tc::mbar_wait(tc::smem_u32(&tempty[buf]), ((t >> 1) & 1) ^ 1, globaltimer_ns() + args.timeout_ns,
+                           s_abort)) {
+          fail(args, s_abort, GEMM_ERR_MMA | 1);
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < kbs; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!tc::mbar_wait(tc::smem_u32(&full[s]), ph, globaltimer_ns() + args.timeout_ns, s_abort)) {
+            fail(args, s_abort, GEMM_ERR_MMA | 2);
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t a0 = tc::smem_u32(sA + s * A_BYTES);
+          const uint32_t b0 = tc::smem_u32(sB + s * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            tc::umma_f16(tmem_d, tc::sw128_kmajor_desc(a0 + k * 32), tc::sw128_kmajor_desc(b0 + k * 32), IDESC,
+                         (kb | k) != 0);
+          }
+          issued = true;
+          tc::umma_commit(tc::smem_u32(&empty[s]));
+        }
+        if (!ok) break;
+        tc::umma_commit(tc::smem_u32(&tfull[buf]));
+      }
+      if ((!ok || *s_abort) && issued) {
+        // Wait for the MMAs already issued before TMEM is released.
+        tc::umma_commit(tc::smem_u32(drain));
+        int never = 0;
+        tc::mbar_wait(tc::smem_u32(drain), 0, globaltimer_ns() + 50000000ull, &never);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // the TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+      int mb, nb;
+      tile_coords(tile, m_tiles, args.n_tiles, mb, nb);
+      const int buf = t & 1;
+      if (!tc::mbar_wait(tc::smem_u32(&tfull[buf]), (t >> 1) & 1, globaltimer_ns() + args.timeout_ns, s_abort)) {
+        fail(args, s_abort, GEMM_ERR_EPI | 1);
+        break;
+      }
+      tc::tc_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
+      const int row = mb * BM + row_in_tile;
+      const int col0 = nb * args.n_tile_cols;
+      if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t g[32], u[32];
+          tc::tmem_ld_32x32b_x32(taddr + c, g);
+          tc::tmem_ld_32x32b_x32(taddr + 128 + c, u);
+          tc::tmem_wait_ld();
+          const int col = col0 + c;
+          if (row < args.M && col < args.N) {
+            uint32_t o[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float v[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const float gb = to_f32(from_f32<__nv_bfloat16>(__uint_as_float(g[2 * j + h])));
+                const float ub = to_f32(from_f32<__nv_bfloat16>(__uint_as_float(u[2 * j + h])));
+                const float sb = to_f32(from_f32<__nv_bfloat16>(gb / (1.f + __expf(-gb))));
+                v[h] = sb * ub;
+              }
+              o[j] = pack_bf16(v[0], v[1]);
+            }
+            __nv_bfloat16* dst = args.D + (int64_t)row * args.ldd + col;
+            if (col + 32 <= args.N) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<uint4*>(dst)[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+            } else {
+              const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(o);
+              for (int j = 0; j < 32 && col + j < args.N; ++j) dst[j] = ob[j];
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tc::tmem_ld_32x32b_x32(taddr + c, r);
+          tc::tmem_wait_ld();
+          const int col = col0 + c;
+          if (row < args.M && col < args.N) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            if constexpr (EPI == EPI_RESIDUAL) {
+              const __nv_bfloat16* rp = args.R + (int64_t)row * args.ldr + col;
+              if (col + 32 <= args.N) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  float rv[8];
+                  Vec8IO<__nv_bfloat16>::load(rp + 8 * j, rv);
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) v[8 * j + i] = to_f32(from_f32<__nv_bfloat16>(v[8 * j + i])) + rv[i];
+                }
+              } else {
+                for (int j = 0; j < 32 && col + j < args.N; ++j)
+                  v[j] = to_f32(from_f32<__nv_bfloat16>(v[j])) + to_f32(rp[j]);
+              }
+            }
+            __nv_bfloat16* dst = args.D + (int64_t)row * args.ldd + col;
+            if (col + 32 <= args.N) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<uint4*>(dst)[j] =
+                    make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                               pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+            } else {
+              for (int j = 0; j < 32 && col + j < args.N; ++j) dst[j] = from_f32<__nv_bfloat16>(v[j]);
+            }
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(tc::smem_u32(&tempty[buf]));
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
+                "gemm: cuTensorMapEncodeTiled is unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix (row stride ld elements),
+// box = box_rows x 64 columns, 128-byte swizzle, out-of-range elements read as zero.
+CUtensorMap make_tmap(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "gemm: cuTensorMapEncodeTiled failed (", (int)r, ")");
+  return m;
+}
+
+int* status_word() {
+  static int* p = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = nullptr;
+    TORCH_CHECK(cudaHostAlloc(&h, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) == cudaSuccess,
+                "gemm: cudaHostAlloc(status) failed");
+    *reinterpret_cast<volatile int*>(h) = 0;
+    p = reinterpret_cast<int*>(h);
+  });
+  return p;
+}
+
+int sm_count(int dev) {
+  static int cached[64] = {0};
+  if (cached[dev] == 0) cudaDeviceGetAttribute(&cached[dev], cudaDevAttrMultiProcessorCount, dev);
+  return cached[dev];
+}
+
+template <int EPI>
+void launch(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const at::Tensor* R, int M, int N, int K,
+            double timeout_ms, int max_ctas) {
+  static bool attr_set[64] = {false};
+  const int dev = A.get_device();
+  auto kern = gemm_bf16_kernel<EPI>;
+  if (!attr_set[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  GemmArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  if (EPI == EPI_SWIGLU) {
+    a.n_tile_cols = 128;
+    a.b_first_step = 128;
+    a.b_second = N;  // up rows start at I
+  } else {
+    a.n_tile_cols = BN;
+    a.b_first_step = BN;
+    a.b_second = 128;
+  }
+  a.n_tiles = (N + a.n_tile_cols - 1) / a.n_tile_cols;
+  a.D = reinterpret_cast<__nv_bfloat16*>(D.data_ptr());
+  a.ldd = (int)D.stride(0);
+  a.R = R ? reinterpret_cast<const __nv_bfloat16*>(R->data_ptr()) : nullptr;
+  a.ldr = R ? (int)R->stride(0) : 0;
+  a.status = status_word();
+  a.timeout_ns = (uint64_t)(timeout_ms * 1e6);
+  const CUtensorMap tA = make_tmap(A.data_ptr(), M, K, A.stride(0), BM);
+  const CUtensorMap tB = make_tmap(B.data_ptr(), B.size(0), K, B.stride(0), 128);
+  const int tiles = ((M + BM - 1) / BM) * a.n_tiles;
+  int grid = std::min(tiles, sm_count(dev));
+  if (max_ctas > 0) grid = std::min(grid, max_ctas);
+  kern<<<grid, NUM_THREADS, SMEM_BYTES, at::cuda::getCurrentCUDAStream()>>>(tA, tB, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void check_operand(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2, "gemm: ", name,
+              " must be a 2-D bf16 CUDA tensor");
+  TORCH_CHECK(t.stride(1) == 1 && (t.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              "gemm: ", name, " must be row-major with 16-byte aligned rows");
+}
+
+}  // namespace gemm
+
+// out = a @ b^T (epi 0), silu(a @ gate^T) * (a @ up^T) with b = [gate; up] (epi 1),
+// a @ b^T + residual (epi 2).
+at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& out_opt, int64_t epi,
+                     const c10::optional<at::Tensor>& residual, double timeout_ms, int64_t max_ctas) {
+  using namespace gemm;
+  check_operand(a, "a");
+  check_operand(b, "b");
+  TORCH_CHECK(a.size(1) == b.size(1), "gemm: K mismatch");
+  const int M = (int)a.size(0), K = (int)a.size(1);
+  int N = (int)b.size(0);
+  if (epi == EPI_SWIGLU) {
+    TORCH_CHECK(N % 2 == 0, "gemm(swiglu): b must stack gate and up rows");
+    N /= 2;
+  }
+  c10::cuda::CUDAGuard guard(a.device());
+  at::Tensor out = out_opt.has_value() ? *out_opt : at::empty({M, N}, a.options());
+  check_operand(out, "out");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm: bad output shape");
+  if (M == 0 || N == 0) return out;
+  if (epi == EPI_RESIDUAL) {
+    TORCH_CHECK(residual.has_value(), "gemm(residual): residual tensor required");
+    check_operand(*residual, "residual");
+    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N, "gemm: bad residual shape");
+  }
+  switch (epi) {
+    case EPI_STORE: launch<EPI_STORE>(a, b, out, nullptr, M, N, K, timeout_ms, (int)max_ctas); break;
+    case EPI_SWIGLU: launch<EPI_SWIGLU>(a, b, out, nullptr, M, N, K, timeout_ms, (int)max_ctas); break;
+    case EPI_RESIDUAL: launch<EPI_RESIDUAL>(a, b, out, &*residual, M, N, K, timeout_ms, (int)max_ctas); break;
+    default: TORCH_CHECK(false, "gemm: unknown epilogue ", epi);
+  }
+  return out;
+}
+
+// Error word of the GEMM kernels (0 = ok); clear = reset it to 0.
+int64_t gemm_status(bool clear) {
+  volatile int* p = gemm::status_word();
+  const int v = *p;
+  if (clear) *p = 0;
+  return v;
+}
+
+}  // namespace qfc

@@ -1,0 +1,335 @@
+// Llama layer kernels for sm_100a: RMSNorm (with fused residual add), rotary embedding
+// with the paged KV-cache write, SwiGLU, token embedding and greedy argmax.
+//
+// In the reference these come from Hugging Face modules (LlamaRMSNorm, rotary embedding,
+// nn.SiLU in model.py:27 and the elementwise multiply at model.py:34); here each is one
+// memory-bound kernel with 16-byte accesses, launched on the caller's stream.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAException.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace qfc {
+
+namespace {
+
+template <int NT>
+QFC_DEV float block_sum(float v, float* smem) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(QFC_FULL_MASK, v, off);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) smem[warp] = v;
+  __syncthreads();
+  float t = (lane < NT / 32) ? smem[lane] : 0.f;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(QFC_FULL_MASK, t, off);
+  return t;
+}
+
+// y = rmsnorm(x + residual) * w;  when residual is given, x + residual is also written to
+// residual_out (the new residual stream).  One CTA per row, up to 8 x 8 elements/thread
+// held in registers.  Rounding follows the HF module: normalise in fp32, round to the
+// activation dtype, then multiply by the weight and round again.
+template <typename T, int NT, int VPT>
+__global__ void __launch_bounds__(NT)
+rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ residual, T* __restrict__ residual_out,
+               const T* __restrict__ w, T* __restrict__ y, int H, float eps) {
+  __shared__ float smem[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * H;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int c = (k * NT + threadIdx.x) * 8;
+    if (c < H) {
+      Vec8IO<T>::load(xr + c, v[k]);
+      if (residual != nullptr) {
+        float r[8];
+        Vec8IO<T>::load(residual + row * H + c, r);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[k][i] = to_f32(from_f32<T>(v[k][i] + r[i]));
+        Vec8IO<T>::store(residual_out + row * H + c, v[k]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[k][i] * v[k][i];
+    }
+  }
+  const float tot = block_sum<NT>(ss, smem);
+  const float r = rsqrtf(tot / (float)H + eps);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int c = (k * NT + threadIdx.x) * 8;
+    if (c < H) {
+      float wv[8];
+      Vec8IO<T>::load(w + c, wv);
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = to_f32(from_f32<T>(v[k][i] * r)) * wv[i];
+      Vec8IO<T>::store(y + row * H + c, o);
+    }
+  }
+}
+
+// Rotary embedding (rotate-half convention) applied in place to q and k of the fused
+// qkv activation [M, (nq + 2*nkv) * hd], and k / v copied into the paged cache
+// k_cache / v_cache [num_pages, nkv, page, hd] at slot_mapping[m] (page * page_size +
+// offset; negative = do not cache).  One warp per (token, head); hd = 64 or 128.
+template <typename T>
+__global__ void rope_kv_kernel(T* __restrict__ qkv, const int64_t* __restrict__ pos, const float2* __restrict__ cs,
+                               T* __restrict__ k_cache, T* __restrict__ v_cache,
+                               const int64_t* __restrict__ slot_mapping, int64_t M, int nq, int nkv, int hd,
+                               int page) {
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int heads = nq + 2 * nkv;
+  if (gw >= M * heads) return;
+  const int64_t m = gw / heads;
+  const int h = (int)(gw % heads);
+  T* row = qkv + m * (int64_t)heads * hd + (int64_t)h * hd;
+  const int half = hd >> 1;
+  if (h < nq + nkv) {
+    const float2* c = cs + pos[m] * half;
+    for (int i = lane; i < half; i += 32) {
+      const float2 a = c[i];  // (cos, sin)
+      const float x1 = to_f32(row[i]), x2 = to_f32(row[i + half]);
+      row[i] = from_f32<T>(x1 * a.x - x2 * a.y);
+      row[i + half] = from_f32<T>(x2 * a.x + x1 * a.y);
+    }
+  }
+  if (h >= nq && slot_mapping != nullptr) {
+    const int64_t slot = slot_mapping[m];
+    if (slot >= 0) {
+      __syncwarp();
+      const int64_t pg = slot / page, off = slot % page;
+      const int kvh = (h < nq + nkv) ? h - nq : h - nq - nkv;
+      T* dst = (h < nq + nkv ? k_cache : v_cache) + ((pg * nkv + kvh) * (int64_t)page + off) * hd;
+      for (int i = lane; i < hd; i += 32) dst[i] = row[i];
+    }
+  }
+}
+
+// out[m, j] = silu(gu[m, j]) * gu[m, I + j] for the fused gate|up activation [M, 2I].
+template <typename T>
+__global__ void silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t M, int I) {
+  const int64_t per_row = I / 8;
+  const int64_t total = M * per_row;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = t / per_row;
+    const int64_t j = (t % per_row) * 8;
+    float g[8], u[8], o[8];
+    Vec8IO<T>::load(gu + m * 2 * I + j, g);
+    Vec8IO<T>::load(gu + m * 2 * I + I + j, u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      // HF order: act_fn(gate) is rounded to the activation dtype before the multiply.
+      const float s = to_f32(from_f32<T>(g[i] / (1.f + __expf(-g[i]))));
+      o[i] = s * u[i];
+    }
+    Vec8IO<T>::store(out + m * I + j, o);
+  }
+}
+
+template <typename T>
+__global__ void embedding_kernel(const int64_t* __restrict__ ids, const T* __restrict__ table, T* __restrict__ out,
+                                 int64_t M, int H, int64_t vocab_start, int64_t vocab_end) {
+  const int64_t per_row = H / 8;
+  const int64_t total = M * per_row;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = t / per_row;
+    const int64_t j = (t % per_row) * 8;
+    const int64_t id = ids[m];
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (id >= vocab_start && id < vocab_end)
+      v = *reinterpret_cast<const uint4*>(table + (id - vocab_start) * H + j);
+    *reinterpret_cast<uint4*>(out + m * H + j) = v;
+  }
+}
+
+// Row-wise (max value, argmax) over logits [M, V] (first index wins ties).
+template <typename T>
+__global__ void argmax_kernel(const T* __restrict__ logits, float* __restrict__ best_val, int64_t* __restrict__ best_idx,
+                              int64_t V, int64_t idx_offset) {
+  const int64_t row = blockIdx.x;
+  const T* r = logits + row * V;
+  float bv = -FLT_MAX;
+  int64_t bi = INT64_MAX;
+  for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = to_f32(r[i]);
+    if (v > bv || (v == bv && i < bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int64_t si[32];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(QFC_FULL_MASK, bv, off);
+    const int64_t oi = __shfl_xor_sync(QFC_FULL_MASK, bi, off);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    bv = lane < nw ? sv[lane] : -FLT_MAX;
+    bi = lane < nw ? si[lane] : INT64_MAX;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(QFC_FULL_MASK, bv, off);
+      const int64_t oi = __shfl_xor_sync(QFC_FULL_MASK, bi, off);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      best_val[row] = bv;
+      best_idx[row] = bi + idx_offset;
+    }
+  }
+}
+
+#define QFC_DISPATCH_16(dt, ...)                                          \
+  do {                                                                    \
+    if ((dt) == at::kBFloat16) {                                          \
+      using scalar_t = __nv_bfloat16;                                     \
+      __VA_ARGS__();                                                      \
+    } else if ((dt) == at::kHalf) {                                       \
+      using scalar_t = __half;                                            \
+      __VA_ARGS__();                                                      \
+    } else {                                                              \
+      TORCH_CHECK(false, "expected a bf16 or fp16 tensor, got ", (dt));   \
+    }                                                                     \
+  } while (0)
+
+}  // namespace
+
+// y = rmsnorm(x [+ residual]) * w; when residual is given, residual is updated in place
+// to x + residual.
+void rmsnorm_cuda(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& y,
+                  double eps) {
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && y.is_contiguous() && w.is_contiguous(), "rmsnorm: contiguous CUDA tensors");
+  const int H = (int)x.size(-1);
+  const int64_t M = x.numel() / H;
+  TORCH_CHECK(H % 8 == 0 && H <= 8 * 8 * 1024, "rmsnorm: hidden size must be a multiple of 8, <= 65536");
+  if (M == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const bool has_res = residual.has_value() && residual->defined();
+  QFC_DISPATCH_16(x.scalar_type(), [&] {
+    const scalar_t* rp = has_res ? reinterpret_cast<const scalar_t*>(residual->data_ptr()) : nullptr;
+    scalar_t* ro = has_res ? reinterpret_cast<scalar_t*>(residual->data_ptr()) : nullptr;
+    auto xp = reinterpret_cast<const scalar_t*>(x.data_ptr());
+    auto wp = reinterpret_cast<const scalar_t*>(w.data_ptr());
+    auto yp = reinterpret_cast<scalar_t*>(y.data_ptr());
+    const int vec = H / 8;
+    if (vec <= 512) {
+      constexpr int NT = 512;
+      rmsnorm_kernel<scalar_t, NT, 1><<<M, NT, 0, st>>>(xp, rp, ro, wp, yp, H, (float)eps);
+    } else if (vec <= 1024) {
+      constexpr int NT = 512;
+      rmsnorm_kernel<scalar_t, NT, 2><<<M, NT, 0, st>>>(xp, rp, ro, wp, yp, H, (float)eps);
+    } else {
+      constexpr int NT = 1024;
+      rmsnorm_kernel<scalar_t, NT, 8><<<M, NT, 0, st>>>(xp, rp, ro, wp, yp, H, (float)eps);
+    }
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rope_kv_cuda(at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& cos_sin, const c10::optional<at::Tensor>& k_cache,
+                  const c10::optional<at::Tensor>& v_cache, const c10::optional<at::Tensor>& slot_mapping, int64_t nq,
+                  int64_t nkv, int64_t hd) {
+  TORCH_CHECK(qkv.is_cuda() && qkv.is_contiguous(), "rope_kv: contiguous CUDA qkv");
+  TORCH_CHECK(pos.scalar_type() == at::kLong && cos_sin.scalar_type() == at::kFloat, "rope_kv: int64 positions, fp32 cos/sin");
+  const int64_t M = qkv.numel() / ((nq + 2 * nkv) * hd);
+  if (M == 0) return;
+  c10::cuda::CUDAGuard guard(qkv.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const bool cache = slot_mapping.has_value() && slot_mapping->defined();
+  int page = 1;
+  if (cache) {
+    TORCH_CHECK(k_cache->dim() == 4, "rope_kv: cache must be [pages, nkv, page, hd]");
+    page = (int)k_cache->size(2);
+  }
+  const int64_t warps = M * (nq + 2 * nkv);
+  const int threads = 256;
+  const int64_t blocks = (warps * 32 + threads - 1) / threads;
+  QFC_DISPATCH_16(qkv.scalar_type(), [&] {
+    rope_kv_kernel<scalar_t><<<blocks, threads, 0, st>>>(
+        reinterpret_cast<scalar_t*>(qkv.data_ptr()), pos.data_ptr<int64_t>(),
+        reinterpret_cast<const float2*>(cos_sin.data_ptr()),
+        cache ? reinterpret_cast<scalar_t*>(k_cache->data_ptr()) : nullptr,
+        cache ? reinterpret_cast<scalar_t*>(v_cache->data_ptr()) : nullptr,
+        cache ? slot_mapping->data_ptr<int64_t>() : nullptr, M, (int)nq, (int)nkv, (int)hd, page);
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void silu_mul_cuda(const at::Tensor& gu, at::Tensor& out) {
+  TORCH_CHECK(gu.is_contiguous() && out.is_contiguous(), "silu_mul: contiguous tensors");
+  const int I = (int)out.size(-1);
+  const int64_t M = out.numel() / I;
+  TORCH_CHECK(gu.size(-1) == 2 * I && I % 8 == 0, "silu_mul: gu must be [M, 2I], I % 8 == 0");
+  if (M == 0) return;
+  c10::cuda::CUDAGuard guard(gu.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int64_t total = M * (I / 8);
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+  QFC_DISPATCH_16(gu.scalar_type(), [&] {
+    silu_mul_kernel<scalar_t><<<blocks, 256, 0, st>>>(reinterpret_cast<const scalar_t*>(gu.data_ptr()),
+                                                       reinterpret_cast<scalar_t*>(out.data_ptr()), M, I);
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void embedding_cuda(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t vocab_start) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && table.is_contiguous() && out.is_contiguous(), "embedding: bad args");
+  const int H = (int)table.size(1);
+  const int64_t M = ids.numel();
+  TORCH_CHECK(H % 8 == 0, "embedding: hidden size must be a multiple of 8");
+  if (M == 0) return;
+  c10::cuda::CUDAGuard guard(table.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int64_t total = M * (H / 8);
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+  QFC_DISPATCH_16(table.scalar_type(), [&] {
+    embedding_kernel<scalar_t><<<blocks, 256, 0, st>>>(ids.data_ptr<int64_t>(), reinterpret_cast<const scalar_t*>(table.data_ptr()),
+                                                        reinterpret_cast<scalar_t*>(out.data_ptr()), M, H, vocab_start,
+                                                        vocab_start + table.size(0));
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void argmax_cuda(const at::Tensor& logits, at::Tensor& best_val, at::Tensor& best_idx, int64_t idx_offset) {
+  TORCH_CHECK(logits.is_contiguous() && logits.dim() == 2, "argmax: contiguous [M, V] logits");
+  const int64_t M = logits.size(0), V = logits.size(1);
+  if (M == 0) return;
+  c10::cuda::CUDAGuard guard(logits.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  auto launch = [&](auto tag) {
+    using T = decltype(tag);
+    argmax_kernel<T><<<M, 1024, 0, st>>>(reinterpret_cast<const T*>(logits.data_ptr()), best_val.data_ptr<float>(),
+                                         best_idx.data_ptr<int64_t>(), V, idx_offset);
+  };
+  if (logits.scalar_type() == at::kBFloat16) launch(__nv_bfloat16());
+  else if (logits.scalar_type() == at::kHalf) launch(__half());
+  else if (logits.scalar_type() == at::kFloat) launch(float());
+  else TORCH_CHECK(false, "argmax: unsupported dtype");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace qfc

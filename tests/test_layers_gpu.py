@@ -1,0 +1,78 @@
+"""Layer kernels (RMSNorm, RoPE + KV cache, SwiGLU, embedding, argmax) vs torch."""
+import pytest
+import torch
+
+from quantized_flash_communication_b200.ops import layers as L
+
+pytestmark = pytest.mark.gpu
+
+
+def _rms_ref(x, w, eps):
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return w * y.to(x.dtype)
+
+
+@pytest.mark.parametrize("H", [4096, 8192, 3072, 5120])
+def test_rmsnorm(cuda_device, H):
+    x = torch.randn(37, H, device=cuda_device, dtype=torch.bfloat16)
+    w = torch.randn(H, device=cuda_device, dtype=torch.bfloat16)
+    y = L.rmsnorm(x, w, 1e-5)
+    assert torch.allclose(y.float(), _rms_ref(x, w, 1e-5).float(), rtol=2e-2, atol=2e-2)
+    r = torch.randn_like(x)
+    h = x + r
+    r2 = r.clone()
+    y2 = L.rmsnorm(x, w, 1e-5, residual=r2)
+    assert torch.equal(r2, h)
+    assert torch.allclose(y2.float(), _rms_ref(h, w, 1e-5).float(), rtol=2e-2, atol=2e-2)
+
+
+def _rope_ref(x, pos, cs):
+    # x [M, heads, hd]
+    hd = x.shape[-1]
+    c = cs[pos, :, 0].unsqueeze(1)
+    s = cs[pos, :, 1].unsqueeze(1)
+    x1, x2 = x[..., : hd // 2].float(), x[..., hd // 2:].float()
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+def test_rope_and_cache(cuda_device):
+    nq, nkv, hd, M, page = 8, 2, 128, 50, 16
+    cs = L.rope_cos_sin(4096, hd, 10000.0, cuda_device)
+    qkv = torch.randn(M, (nq + 2 * nkv) * hd, device=cuda_device, dtype=torch.bfloat16)
+    pos = torch.randint(0, 4096, (M,), device=cuda_device)
+    orig = qkv.clone().view(M, nq + 2 * nkv, hd)
+    kc = torch.zeros(8, nkv, page, hd, device=cuda_device, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(8 * page, device=cuda_device)[:M]
+    L.rope_kv(qkv, pos, cs, nq, nkv, hd, kc, vc, slots)
+    out = qkv.view(M, nq + 2 * nkv, hd)
+    ref_q = _rope_ref(orig[:, :nq], pos, cs)
+    ref_k = _rope_ref(orig[:, nq:nq + nkv], pos, cs)
+    assert torch.allclose(out[:, :nq].float(), ref_q, atol=2e-2, rtol=2e-2)
+    assert torch.allclose(out[:, nq:nq + nkv].float(), ref_k, atol=2e-2, rtol=2e-2)
+    assert torch.equal(out[:, nq + nkv:], orig[:, nq + nkv:])
+    pg, off = slots // page, slots % page
+    assert torch.equal(kc[pg, :, off], out[:, nq:nq + nkv])
+    assert torch.equal(vc[pg, :, off], out[:, nq + nkv:])
+
+
+def test_silu_mul(cuda_device):
+    gu = torch.randn(33, 2 * 1376, device=cuda_device, dtype=torch.bfloat16)
+    y = L.silu_mul(gu)
+    ref = torch.nn.functional.silu(gu[:, :1376]) * gu[:, 1376:]
+    assert torch.allclose(y.float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
+def test_embedding_and_argmax(cuda_device):
+    table = torch.randn(1000, 256, device=cuda_device, dtype=torch.bfloat16)
+    ids = torch.randint(0, 2000, (64,), device=cuda_device)
+    y = L.embedding(ids, table, vocab_start=500)
+    for i, t in enumerate(ids.tolist()):
+        if 500 <= t < 1500:
+            assert torch.equal(y[i], table[t - 500])
+        else:
+            assert bool((y[i] == 0).all())
+    logits = torch.randn(7, 32000, device=cuda_device, dtype=torch.bfloat16)
+    bv, bi = L.argmax(logits, idx_offset=100)
+    assert torch.equal(bi - 100, logits.float().argmax(-1))
