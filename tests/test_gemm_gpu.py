@@ -11,7 +11,7 @@ def _ref(a, b):
     return a.float() @ b.float().T
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (1, 256, 64), (100, 300, 136),
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (1, 256, 64), (100, 312, 136),
                                    (1000, 1536, 4096), (8192, 4096, 512), (513, 2752, 1376), (64, 4096, 4096)])
 def test_gemm_store(cuda_device, M, N, K):
     torch.manual_seed(M + N + K)
