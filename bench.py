@@ -1,0 +1,299 @@
+"""Flagship benchmark: tensor-parallel Llama-2-7B prefill (TTFT) on N GPUs of one node.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+Llama-2-7B architecture (32 layers, hidden 4096, 32 heads, SwiGLU
+11008, vocab 32000), bf16 random-init N(0, 0.02) weights, batch 8 x 1024 uniformly random
+token ids, an INT8 (group 128) quantized all-reduce after o_proj and down_proj.  One step
+is one prefill of the whole batch up to the first generated token (TTFT); ``value`` is
+the job's prefill throughput in tokens/s (batch * seq / TTFT).  Timing: W untimed steps,
+then K steps between a barrier + synchronize on both sides, CUDA events on the
+launching stream, maximum over ranks.
+
+``--impl reference`` runs the unmodified reference (baseline/_ref): Hugging Face
+LlamaForCausalLM with the same architecture and init, the reference's
+``inject_ultimate_layers`` (MLP-only tensor parallelism) and its ``flash_all_reduce``
+in INT8 / group 128 / asym mode, in fp16 (its all-reduce always returns fp16).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+import types
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", default="llama2-7b")
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--seq", type=int, default=1024)
+    ap.add_argument("--bits", type=int, default=8)
+    ap.add_argument("--group-size", type=int, default=128)
+    ap.add_argument("--quant-type", default="asym")
+    ap.add_argument("--ar-backend", default="qfc", choices=["qfc", "nccl", "staged"])
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def _dist_init(args):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1 or args.impl == "reference":
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        os.environ.setdefault("RANK", str(rank))
+        os.environ.setdefault("WORLD_SIZE", str(world))
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=600),
+                                device_id=dev)
+    return rank, world, dev
+
+
+def _max_over_ranks(x: float, dev) -> float:
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier():
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+
+
+def _timed(step_fn, args, dev, rank, world):
+    """Warm up, then time K steps on the device (events), max over ranks."""
+    import torch
+    from quantized_flash_communication_b200.utils.clocks import ClockSampler
+    for _ in range(args.warmup):
+        step_fn()
+    torch.cuda.synchronize()
+    _barrier()
+    torch.cuda.synchronize()
+    gpus = list(range(world)) if world > 1 else [dev.index]
+    sampler = ClockSampler(gpus) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        step_fn()
+    e.record()
+    torch.cuda.synchronize()
+    _barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.__exit__(None, None, None)
+    ms = _max_over_ranks(s.elapsed_time(e), dev) / args.steps
+    return ms, (sampler.summary() if sampler else None)
+
+
+def _timed_e2e(step_fn, args, dev):
+    """Host-timed steps that include the pinned H2D input copy and the D2H result read."""
+    import torch
+    for _ in range(1):
+        step_fn()
+    torch.cuda.synchronize()
+    _barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        step_fn()
+    t1 = time.perf_counter()
+    _barrier()
+    return _max_over_ranks((t1 - t0) * 1000.0 / args.e2e_steps, dev)
+
+
+# ------------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    sys.path.insert(0, ROOT)
+    from quantized_flash_communication_b200._ext import count_launches
+    from quantized_flash_communication_b200.models.config import get_config
+    from quantized_flash_communication_b200.models.llama import LlamaTP, TPContext
+    from quantized_flash_communication_b200.ops import attention as A
+    from quantized_flash_communication_b200.ops.gemm import gemm_status
+
+    rank, world, dev = _dist_init(args)
+    cfg = get_config(args.model)
+    B, S = args.batch, args.seq
+    tp = TPContext(None, dev, ar_backend=args.ar_backend, bits=args.bits, group_size=args.group_size,
+                   quant_type=args.quant_type, algo="auto", reserve_tokens=B * S, hidden_size=cfg.hidden_size)
+    model = LlamaTP(cfg, tp, dev, init="shard", seed=1234)
+    g = torch.Generator(device="cpu").manual_seed(42)
+    ids_host = torch.randint(0, cfg.vocab_size, (B, S), generator=g).pin_memory()
+    ids = ids_host.to(dev)
+    cache = model.new_cache(B, S)
+
+    def step():
+        return model.prefill(ids, cache)
+
+    ms, clocks = _timed(step, args, dev, rank, world)
+    torch.cuda.synchronize()
+    with count_launches() as cnt:
+        step()
+    torch.cuda.synchronize()
+    launches_per_step = cnt["kernels"]
+    if tp.ar is not None:
+        tp.ar.check()
+    assert gemm_status() == 0, "a GEMM kernel reported a pipeline timeout"
+
+    e2e = None
+    if not args.no_e2e:
+        out_host = torch.empty(B, dtype=torch.int64).pin_memory()
+
+        def e2e_step():
+            d = ids_host.to(dev, non_blocking=True)
+            nxt = model.prefill(d, cache)
+            out_host.copy_(nxt, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            return out_host
+
+        e2e_ms = _timed_e2e(e2e_step, args, dev)
+        e2e = {"value": B * S / (e2e_ms / 1000.0), "unit": "tokens/s", "ttft_ms": e2e_ms,
+               "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(),
+               "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+               "api": "LlamaTP.prefill"}
+    weights_gb = sum(p.numel() * p.element_size() for p in model.parameters()) / 1e9
+    res = {
+        "metric": "tp_prefill_throughput_llama2_7b",
+        "value": B * S / (ms / 1000.0),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "ttft_ms": ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: uniform random token ids, random-init N(0,0.02) weights",
+        "config": {"model": cfg.name, "global_batch": B, "seq_len": S, "parallelism": f"tp{world}",
+                   "allreduce": (f"qfc fused INT{args.bits} g{args.group_size} {args.quant_type}"
+                                 if args.ar_backend == "qfc" else args.ar_backend) if world > 1 else "none (tp1)",
+                   "attention": A.prefill_backend(),
+                   "l2": f"no flush; each step streams {weights_gb:.1f} GB of weights per rank (> 126 MB L2)"},
+        "clocks": clocks,
+        "e2e": e2e,
+        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches_per_step": launches_per_step,
+        "impl": "ours",
+    }
+    return rank, res
+
+
+# ------------------------------------------------------------------------------------------
+def run_reference(args):
+    import torch
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref, "communication.py")):
+        return 0, {"impl": "reference", "unavailable": "baseline/_ref is missing (copy the reference's 7 .py files)"}
+    rank, world, dev = _dist_init(args)
+    # The reference's main.py imports a `utils` module that it does not ship (main.py:17);
+    # provide the three names it imports so its own inject_ultimate_layers can be used.
+    stub = types.ModuleType("utils")
+    stub.setup_ddp = lambda *a, **k: None
+    stub.cleanup_ddp = lambda *a, **k: None
+    stub.set_seed = lambda s=42: torch.manual_seed(s)
+    sys.modules["utils"] = stub
+    sys.path.insert(0, ref)
+    import main as ref_main  # noqa: E402  (reference, unmodified)
+    from transformers import LlamaConfig as HFConfig, LlamaForCausalLM
+
+    sys.path.insert(1, ROOT)
+    from quantized_flash_communication_b200.models.config import get_config
+    cfg = get_config(args.model)
+    hf = HFConfig(hidden_size=cfg.hidden_size, intermediate_size=cfg.intermediate_size,
+                  num_hidden_layers=cfg.num_layers, num_attention_heads=cfg.num_heads,
+                  num_key_value_heads=cfg.num_kv_heads, vocab_size=cfg.vocab_size, rms_norm_eps=cfg.rms_eps,
+                  rope_theta=cfg.rope_theta, max_position_embeddings=cfg.max_position, initializer_range=0.02,
+                  tie_word_embeddings=False)
+    torch.manual_seed(1234)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.float16)
+    with torch.device(dev):
+        model = LlamaForCausalLM(hf)
+    torch.set_default_dtype(prev)
+    model.eval()
+    ref_main.inject_ultimate_layers(model, rank, world)
+    for layer in model.model.layers:
+        layer.mlp.mode = "flash"
+        layer.mlp.bits = args.bits
+        layer.mlp.group_size = args.group_size
+        layer.mlp.quant_type = args.quant_type
+    B, S = args.batch, args.seq
+    g = torch.Generator(device="cpu").manual_seed(42)
+    ids_host = torch.randint(0, cfg.vocab_size, (B, S), generator=g).pin_memory()
+    ids = ids_host.to(dev)
+
+    def step():
+        with torch.no_grad():
+            return model(ids).logits
+
+    ms, clocks = _timed(step, args, dev, rank, world)
+    e2e = None
+    if not args.no_e2e:
+        def e2e_step():
+            d = ids_host.to(dev, non_blocking=True)
+            with torch.no_grad():
+                nxt = model(d).logits[:, -1].argmax(-1)
+            return nxt.cpu()
+        e2e_ms = _timed_e2e(e2e_step, args, dev)
+        e2e = {"value": B * S / (e2e_ms / 1000.0), "unit": "tokens/s", "ttft_ms": e2e_ms,
+               "h2d_bytes_per_step": ids_host.numel() * 8, "d2h_bytes_per_step": B * 8,
+               "api": "reference: LlamaForCausalLM + inject_ultimate_layers + flash_all_reduce"}
+    res = {
+        "metric": "tp_prefill_throughput_llama2_7b", "value": B * S / (ms / 1000.0), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "ttft_ms": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic: uniform random token ids, random-init N(0,0.02) weights",
+        "config": {"model": cfg.name, "global_batch": B, "seq_len": S, "parallelism": f"tp{world} (MLP only)",
+                   "allreduce": f"reference flash_all_reduce INT{args.bits} g{args.group_size} {args.quant_type}"},
+        "clocks": clocks, "e2e": e2e, "impl": "reference",
+    }
+    return rank, res
+
+
+def main():
+    args = _parse()
+    try:
+        rank, res = run_reference(args) if args.impl == "reference" else run_ours(args)
+    except SystemExit:
+        raise
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    try:
+        import torch.distributed as dist
+        if dist.is_available() and dist.is_initialized():
+            from quantized_flash_communication_b200.communication import reset_communicators
+            reset_communicators()
+            dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+if __name__ == "__main__":
+    main()

@@ -40,6 +40,9 @@ void rope_kv_cuda(at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& cos_
 void silu_mul_cuda(const at::Tensor& gu, at::Tensor& out);
 void embedding_cuda(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t vocab_start);
 void argmax_cuda(const at::Tensor& logits, at::Tensor& best_val, at::Tensor& best_idx, int64_t idx_offset);
+// attn_decode.cu
+void attn_decode_cuda(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& bt,
+                      const at::Tensor& sl, at::Tensor& out, int64_t nq, int64_t nkv, int64_t hd, double scale);
 }  // namespace qfc
 
 namespace py = pybind11;
@@ -86,6 +89,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("silu_mul", &qfc::silu_mul_cuda);
   m.def("embedding", &qfc::embedding_cuda);
   m.def("argmax", &qfc::argmax_cuda);
+  m.def("attn_decode", &qfc::attn_decode_cuda, "paged split-KV decode attention");
 
   m.def("ar_plan", &qfc::ar_plan, "region sizes a quantized all-reduce call needs");
   m.def("quant_all_reduce", &qfc::quant_all_reduce, "fused quantized all-reduce over peer memory",

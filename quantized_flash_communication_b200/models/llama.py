@@ -1,0 +1,349 @@
+"""Tensor-parallel Llama (Llama-2 / Llama-3 architectures) on the sm_100a kernels.
+
+The reference tensor-parallelises only the MLP of a Hugging Face model and replicates
+attention on every rank (model.py:8-57, main.py:25-39).  This model shards the whole
+decoder layer Megatron-style, one process per GPU:
+
+* q/k/v projections column-parallel by head, o_proj row-parallel;
+* gate/up column-parallel, down_proj row-parallel;
+* embedding replicated, lm_head vocab-parallel (argmax combined across ranks);
+* one all-reduce after o_proj and one after down_proj, through the fused quantized
+  kernel (``parallel/quant_allreduce.py``), NCCL (baseline) or nothing at TP=1.
+
+Parameters carry Hugging Face's state-dict names (``model.layers.{i}.self_attn.q_proj
+.weight`` ...) holding this rank's shard; q/k/v and gate/up are views into one fused
+buffer per layer, which the fused GEMMs read.  Every op on the forward path is a kernel
+of this package: tcgen05 GEMMs (with SwiGLU / residual epilogues), RMSNorm with fused
+residual add, RoPE + paged KV-cache write, attention, embedding and argmax.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from ..ops import attention as A
+from ..ops import gemm as G
+from ..ops import layers as L
+from ..parallel.quant_allreduce import QuantAllReduce
+from .config import LlamaConfig, get_config
+
+__all__ = ["TPContext", "LlamaTP", "KVCache", "smoke_forward"]
+
+
+# ------------------------------------------------------------------------------------------
+# Tensor-parallel context
+# ------------------------------------------------------------------------------------------
+class TPContext:
+    """Process group of a tensor-parallel model and the all-reduce it uses.
+
+    ``ar_backend``: "qfc" (fused quantized kernel over peer memory), "nccl" (bf16 NCCL
+    all-reduce, the baseline) or "staged" (the reference's collective structure).
+    ``bits``: 16 / 8 / 6 / 4 as in the reference's flash_all_reduce.
+    """
+
+    def __init__(self, group: Optional[dist.ProcessGroup] = None, device=None, ar_backend: str = "qfc",
+                 bits: int = 8, group_size: int = 128, quant_type: str = "asym", algo: str = "auto",
+                 reserve_tokens: int = 0, hidden_size: int = 0, world: Optional[int] = None,
+                 rank: Optional[int] = None):
+        self.group = group
+        if world is not None:  # explicit (e.g. building one shard offline); no communication
+            self.world, self.rank = world, rank or 0
+            ar_backend = "none" if world > 1 else ar_backend
+        elif dist.is_available() and dist.is_initialized():
+            self.world = dist.get_world_size(group)
+            self.rank = dist.get_rank(group)
+        else:
+            self.world, self.rank = 1, 0
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.ar_backend = ar_backend
+        self.bits = bits
+        self.group_size = group_size
+        self.quant_type = quant_type
+        self.algo = algo
+        self.ar: Optional[QuantAllReduce] = None
+        if self.world > 1 and ar_backend == "qfc":
+            self.ar = QuantAllReduce(group, self.device, bits=bits, group_size=group_size, quant_type=quant_type,
+                                     algo=algo)
+            if reserve_tokens and hidden_size:
+                self.ar.reserve(reserve_tokens * hidden_size, torch.bfloat16, bits_options=(bits, 16))
+
+    def all_reduce(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.world == 1:
+            return x
+        if self.ar_backend == "qfc":
+            return self.ar(x, out=out)
+        if self.ar_backend == "nccl":
+            dist.all_reduce(x, group=self.group)
+            return x
+        if self.ar_backend == "staged":
+            from ..parallel.staged import staged_all_reduce
+            return staged_all_reduce(x, self.bits, self.group_size, self.quant_type, torch.float16, self.group, x.dtype)
+        raise ValueError(f"unknown ar_backend {self.ar_backend!r}")
+
+    def gather_argmax(self, val: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+        """Global argmax from per-rank (max value, index) pairs; ties go to the lower index."""
+        if self.world == 1:
+            return idx
+        B = val.numel()
+        buf = torch.zeros(self.world, B, 2, dtype=torch.float32, device=val.device)
+        buf[self.rank, :, 0] = val
+        buf[self.rank, :, 1] = idx.to(torch.float32)
+        if self.ar is not None:
+            # an all-gather as an exact fp32 sum of disjoint slots, one-shot kernel
+            self.ar(buf, out=buf, bits=16, algo="one_shot")
+        else:
+            dist.all_reduce(buf, group=self.group)
+        best = buf[:, :, 0].argmax(dim=0)  # first maximum = lowest rank
+        return buf[best, torch.arange(B, device=val.device), 1].to(torch.int64)
+
+
+# ------------------------------------------------------------------------------------------
+# KV cache
+# ------------------------------------------------------------------------------------------
+@dataclass
+class KVCache:
+    """Paged KV cache of one rank: per layer [pages, kv_heads, page, head_dim]."""
+    k: list
+    v: list
+    block_table: torch.Tensor  # [B, pages_per_seq] int32
+    seq_lens: torch.Tensor     # [B] int32, tokens already in the cache
+    page: int
+
+    @staticmethod
+    def allocate(n_layers: int, batch: int, max_len: int, nkv: int, hd: int, device, dtype=torch.bfloat16,
+                 page: int = 64) -> "KVCache":
+        pps = (max_len + page - 1) // page
+        pages = batch * pps
+        k = [torch.empty(pages, nkv, page, hd, device=device, dtype=dtype) for _ in range(n_layers)]
+        v = [torch.empty(pages, nkv, page, hd, device=device, dtype=dtype) for _ in range(n_layers)]
+        bt = torch.arange(pages, device=device, dtype=torch.int32).view(batch, pps)
+        return KVCache(k, v, bt, torch.zeros(batch, device=device, dtype=torch.int32), page)
+
+    def slots(self, b_idx: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        pg = self.block_table[b_idx, (pos // self.page).to(torch.long)].to(torch.int64)
+        return pg * self.page + (pos % self.page).to(torch.int64)
+
+
+# ------------------------------------------------------------------------------------------
+# Modules (weights only; the forward is written against the fused buffers)
+# ------------------------------------------------------------------------------------------
+class _W(nn.Module):
+    def __init__(self, w: torch.Tensor):
+        super().__init__()
+        self.weight = nn.Parameter(w, requires_grad=False)
+
+
+class _Attn(nn.Module):
+    def __init__(self, qkv: torch.Tensor, o: torch.Tensor, nq_rows: int, nkv_rows: int):
+        super().__init__()
+        self.register_buffer("qkv_fused", qkv, persistent=False)
+        self.q_proj = _W(qkv[:nq_rows])
+        self.k_proj = _W(qkv[nq_rows:nq_rows + nkv_rows])
+        self.v_proj = _W(qkv[nq_rows + nkv_rows:])
+        self.o_proj = _W(o)
+
+
+class _MLP(nn.Module):
+    def __init__(self, gate_up: torch.Tensor, down: torch.Tensor, inter: int):
+        super().__init__()
+        self.register_buffer("gate_up_fused", gate_up, persistent=False)
+        self.gate_proj = _W(gate_up[:inter])
+        self.up_proj = _W(gate_up[inter:])
+        self.down_proj = _W(down)
+
+
+class _Layer(nn.Module):
+    def __init__(self, attn: _Attn, mlp: _MLP, ln1: torch.Tensor, ln2: torch.Tensor):
+        super().__init__()
+        self.self_attn = attn
+        self.mlp = mlp
+        self.input_layernorm = _W(ln1)
+        self.post_attention_layernorm = _W(ln2)
+
+
+class _Inner(nn.Module):
+    def __init__(self, embed: torch.Tensor, layers, norm: torch.Tensor):
+        super().__init__()
+        self.embed_tokens = _W(embed)
+        self.layers = nn.ModuleList(layers)
+        self.norm = _W(norm)
+
+
+class LlamaTP(nn.Module):
+    """One rank's shard of a tensor-parallel Llama model (inference)."""
+
+    def __init__(self, cfg: LlamaConfig | str, tp: Optional[TPContext] = None, device=None,
+                 dtype: torch.dtype = torch.bfloat16, init: str = "shard", seed: int = 0, init_std: float = 0.02):
+        super().__init__()
+        cfg = get_config(cfg) if isinstance(cfg, str) else cfg
+        self.cfg = cfg
+        self.tp = tp or TPContext(device=device)
+        W, r = self.tp.world, self.tp.rank
+        device = self.tp.device if device is None else torch.device(device)
+        self.device = device
+        self.dtype = dtype
+        H, hd = cfg.hidden_size, cfg.head_dim
+        assert cfg.num_heads % W == 0, "heads must divide by the TP degree"
+        assert cfg.num_kv_heads % W == 0, "kv heads must divide by the TP degree"
+        assert cfg.intermediate_size % W == 0, "intermediate size must divide by the TP degree"
+        self.nq, self.nkv, self.hd = cfg.num_heads // W, cfg.num_kv_heads // W, hd
+        self.inter = cfg.intermediate_size // W
+        self.v_local = (cfg.vocab_size + W - 1) // W
+        self.vocab_start = r * self.v_local
+
+        def rnd(shape, full_shape=None, slicer=None, key=0):
+            if init == "full":
+                g = torch.Generator(device=device).manual_seed(seed * 1000003 + key)
+                t = torch.empty(full_shape, device=device, dtype=dtype).normal_(0.0, init_std, generator=g)
+                return slicer(t).contiguous()
+            g = torch.Generator(device=device).manual_seed(seed * 1000003 + key * 131 + r)
+            return torch.empty(shape, device=device, dtype=dtype).normal_(0.0, init_std, generator=g)
+
+        nqr, nkvr = self.nq * hd, self.nkv * hd
+        layers = []
+        for i in range(cfg.num_layers):
+            k0 = (i + 1) * 16
+            q = rnd((nqr, H), (cfg.num_heads * hd, H), lambda t: t[r * nqr:(r + 1) * nqr], k0 + 1)
+            k = rnd((nkvr, H), (cfg.num_kv_heads * hd, H), lambda t: t[r * nkvr:(r + 1) * nkvr], k0 + 2)
+            v = rnd((nkvr, H), (cfg.num_kv_heads * hd, H), lambda t: t[r * nkvr:(r + 1) * nkvr], k0 + 3)
+            qkv = torch.cat([q, k, v], 0).contiguous()
+            del q, k, v
+            o = rnd((H, nqr), (H, cfg.num_heads * hd), lambda t: t[:, r * nqr:(r + 1) * nqr], k0 + 4)
+            I = self.inter
+            gate = rnd((I, H), (cfg.intermediate_size, H), lambda t: t[r * I:(r + 1) * I], k0 + 5)
+            up = rnd((I, H), (cfg.intermediate_size, H), lambda t: t[r * I:(r + 1) * I], k0 + 6)
+            gu = torch.cat([gate, up], 0).contiguous()
+            del gate, up
+            down = rnd((H, I), (H, cfg.intermediate_size), lambda t: t[:, r * I:(r + 1) * I], k0 + 7)
+            ones = torch.ones(H, device=device, dtype=dtype)
+            layers.append(_Layer(_Attn(qkv, o, nqr, nkvr), _MLP(gu, down, I), ones.clone(), ones.clone()))
+        emb = rnd((cfg.vocab_size, H), (cfg.vocab_size, H), lambda t: t, 1)
+        self.model = _Inner(emb, layers, torch.ones(H, device=device, dtype=dtype))
+        vpad = self.v_local * W
+        head = rnd((self.v_local, H), (vpad, H), lambda t: t[r * self.v_local:(r + 1) * self.v_local], 2)
+        if self.vocab_start + self.v_local > cfg.vocab_size:  # padded rows never win the argmax
+            head[cfg.vocab_size - self.vocab_start:] = 0
+        self.lm_head = _W(head)
+        self.cos_sin = L.rope_cos_sin(cfg.max_position, hd, cfg.rope_theta, device, cfg.rope_scaling)
+
+    # --------------------------------------------------------------------------------------
+    def new_cache(self, batch: int, max_len: int, page: int = 64) -> KVCache:
+        return KVCache.allocate(self.cfg.num_layers, batch, max_len, self.nkv, self.hd, self.device, self.dtype, page)
+
+    def _layer(self, li: int, h: torch.Tensor, x: torch.Tensor, attn_fn, pos, slots, cache: Optional[KVCache]):
+        """One decoder layer.  h: residual stream [M, H] (updated in place); x: its norm.
+
+        Returns the input norm of the next layer (or the final norm after the last one).
+        """
+        cfg, tp = self.cfg, self.tp
+        lay = self.model.layers[li]
+        eps = cfg.rms_eps
+        qkv = G.linear(x, lay.self_attn.qkv_fused)
+        kc = cache.k[li] if cache is not None else None
+        vc = cache.v[li] if cache is not None else None
+        L.rope_kv(qkv, pos, self.cos_sin, self.nq, self.nkv, self.hd, kc, vc, slots)
+        o = attn_fn(qkv, li)
+        if tp.world == 1:
+            G.linear_residual(o, lay.self_attn.o_proj.weight, h, out=h)
+            x = L.rmsnorm(h, lay.post_attention_layernorm.weight, eps)
+        else:
+            p = G.linear(o, lay.self_attn.o_proj.weight)
+            ar = tp.all_reduce(p, out=p)
+            x = L.rmsnorm(ar, lay.post_attention_layernorm.weight, eps, residual=h)
+        act = G.linear_swiglu(x, lay.mlp.gate_up_fused)
+        nxt = (self.model.layers[li + 1].input_layernorm.weight if li + 1 < cfg.num_layers else self.model.norm.weight)
+        if tp.world == 1:
+            G.linear_residual(act, lay.mlp.down_proj.weight, h, out=h)
+            return L.rmsnorm(h, nxt, eps)
+        p = G.linear(act, lay.mlp.down_proj.weight)
+        ar = tp.all_reduce(p, out=p)
+        return L.rmsnorm(ar, nxt, eps, residual=h)
+
+    def _head(self, x_last: torch.Tensor) -> torch.Tensor:
+        logits = G.linear(x_last, self.lm_head.weight)
+        val, idx = L.argmax(logits, self.vocab_start)
+        return self.tp.gather_argmax(val, idx)
+
+    @torch.no_grad()
+    def prefill(self, ids: torch.Tensor, cache: Optional[KVCache] = None, return_last_hidden: bool = False):
+        """Causal forward over ``ids [B, S]`` (int64, on device); returns greedy next tokens [B].
+
+        With ``cache``, k/v of all positions are written to it and ``seq_lens`` becomes S.
+        """
+        B, S = ids.shape
+        M = B * S
+        cfg = self.cfg
+        h = L.embedding(ids.reshape(-1), self.model.embed_tokens.weight)
+        pos = torch.arange(S, device=self.device, dtype=torch.int64).repeat(B)
+        slots = None
+        if cache is not None:
+            b_idx = torch.arange(B, device=self.device).repeat_interleave(S)
+            slots = cache.slots(b_idx, pos)
+        x = L.rmsnorm(h, self.model.layers[0].input_layernorm.weight, cfg.rms_eps)
+
+        def attn(qkv, li):
+            return A.prefill_attention(qkv, B, S, self.nq, self.nkv, self.hd)
+
+        for li in range(cfg.num_layers):
+            x = self._layer(li, h, x, attn, pos, slots, cache)
+        if cache is not None:
+            cache.seq_lens.fill_(S)
+        x_last = x.view(B, S, -1)[:, -1].contiguous()
+        nxt = self._head(x_last)
+        if return_last_hidden:
+            return nxt, x_last
+        return nxt
+
+    @torch.no_grad()
+    def decode_step(self, tokens: torch.Tensor, cache: KVCache) -> torch.Tensor:
+        """One token per sequence: appends to the cache and returns greedy next tokens [B]."""
+        B = tokens.numel()
+        cfg = self.cfg
+        pos = cache.seq_lens.to(torch.int64)
+        b_idx = torch.arange(B, device=self.device)
+        slots = cache.slots(b_idx, pos)
+        h = L.embedding(tokens.reshape(-1), self.model.embed_tokens.weight)
+        x = L.rmsnorm(h, self.model.layers[0].input_layernorm.weight, cfg.rms_eps)
+        cache.seq_lens.add_(1)
+        nqr = self.nq * self.hd
+
+        def attn(qkv, li):
+            q = qkv[:, :nqr].contiguous()
+            return A.decode_attention(q, cache.k[li], cache.v[li], cache.block_table, cache.seq_lens, self.nq,
+                                      self.nkv, self.hd)
+
+        for li in range(cfg.num_layers):
+            x = self._layer(li, h, x, attn, pos, slots, cache)
+        return self._head(x)
+
+    @torch.no_grad()
+    def generate(self, ids: torch.Tensor, max_new_tokens: int, cache: Optional[KVCache] = None) -> torch.Tensor:
+        """Greedy generation; returns [B, max_new_tokens] new tokens."""
+        B, S = ids.shape
+        if cache is None:
+            cache = self.new_cache(B, S + max_new_tokens)
+        out = torch.empty(B, max_new_tokens, dtype=torch.int64, device=self.device)
+        tok = self.prefill(ids, cache)
+        out[:, 0] = tok
+        for t in range(1, max_new_tokens):
+            tok = self.decode_step(tok, cache)
+            out[:, t] = tok
+        return out
+
+
+def smoke_forward(device) -> None:
+    """One tiny prefill + decode step of the flagship architecture (random weights)."""
+    from .config import LlamaConfig
+    cfg = LlamaConfig("smoke", 1024, 2048, 1, 8, 8, 1024, head_dim=128, max_position=512)
+    m = LlamaTP(cfg, device=device)
+    ids = torch.randint(0, cfg.vocab_size, (2, 64), device=device)
+    cache = m.new_cache(2, 80)
+    tok = m.prefill(ids, cache)
+    tok2 = m.decode_step(tok, cache)
+    torch.cuda.synchronize(device)
+    assert tok.shape == (2,) and tok2.shape == (2,)
+    assert G.gemm_status() == 0

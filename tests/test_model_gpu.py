@@ -1,0 +1,86 @@
+"""Tensor-parallel Llama (TP=1) vs Hugging Face LlamaForCausalLM with the same weights."""
+import pytest
+import torch
+
+from quantized_flash_communication_b200.models.config import get_config
+from quantized_flash_communication_b200.models.llama import LlamaTP, TPContext
+from quantized_flash_communication_b200.quantization import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def _hf(cfg, sd, dev):
+    from transformers import LlamaConfig as HFC, LlamaForCausalLM
+    hfc = HFC(hidden_size=cfg.hidden_size, intermediate_size=cfg.intermediate_size, num_hidden_layers=cfg.num_layers,
+              num_attention_heads=cfg.num_heads, num_key_value_heads=cfg.num_kv_heads, vocab_size=cfg.vocab_size,
+              head_dim=cfg.head_dim, rms_norm_eps=cfg.rms_eps, rope_theta=cfg.rope_theta,
+              max_position_embeddings=cfg.max_position, tie_word_embeddings=False)
+    with torch.device(dev):
+        hf = LlamaForCausalLM(hfc).to(torch.bfloat16)
+    missing, unexpected = hf.load_state_dict(sd, strict=False)
+    assert not unexpected and all("rotary" in k for k in missing)
+    return hf.eval()
+
+
+@pytest.mark.parametrize("name", ["tiny", "tiny-mha"])
+def test_prefill_and_decode_match_hf(cuda_device, name):
+    cfg = get_config(name)
+    m = LlamaTP(cfg, TPContext(device=cuda_device), cuda_device, init="full", seed=11, init_std=0.05)
+    hf = _hf(cfg, m.state_dict(), cuda_device)
+    B, S = 3, 100
+    ids = torch.randint(0, cfg.vocab_size, (B, S), device=cuda_device)
+    cache = m.new_cache(B, S + 4)
+    tok, x_last = m.prefill(ids, cache, return_last_hidden=True)
+    with torch.no_grad():
+        out = hf(ids, output_hidden_states=True)
+    ref_h = out.hidden_states[-1][:, -1]
+    assert rel_l2(x_last.float(), ref_h.float()) < 0.03
+    ref_logits = out.logits[:, -1].float()
+    ours_logits = (x_last.float() @ m.lm_head.weight.float().T)
+    assert rel_l2(ours_logits, ref_logits) < 0.03
+    # greedy tokens agree where the top-2 margin is clear
+    top2 = ref_logits.topk(2, -1).values
+    clear = (top2[:, 0] - top2[:, 1]) > 0.05 * top2[:, 0].abs().clamp_min(1)
+    assert torch.equal(tok[clear], ref_logits.argmax(-1)[clear])
+    # one decode step == HF on the extended sequence
+    tok2 = m.decode_step(tok, cache)
+    with torch.no_grad():
+        out2 = hf(torch.cat([ids, tok.view(B, 1)], 1))
+    ref2 = out2.logits[:, -1].float()
+    top2 = ref2.topk(2, -1).values
+    clear = (top2[:, 0] - top2[:, 1]) > 0.05 * top2[:, 0].abs().clamp_min(1)
+    assert torch.equal(tok2[clear], ref2.argmax(-1)[clear])
+    assert int(cache.seq_lens[0]) == S + 1
+
+
+def test_decode_attention_vs_torch(cuda_device):
+    from quantized_flash_communication_b200.ops.attention import decode_attention
+    B, nq, nkv, hd, page = 5, 16, 4, 128, 64
+    lens = torch.tensor([1, 63, 64, 700, 1500], dtype=torch.int32, device=cuda_device)
+    pps = 24
+    kc = torch.randn(B * pps, nkv, page, hd, device=cuda_device, dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    bt = torch.randperm(B * pps, device=cuda_device, dtype=torch.int32).view(B, pps).contiguous()
+    q = torch.randn(B, nq * hd, device=cuda_device, dtype=torch.bfloat16)
+    o = decode_attention(q, kc, vc, bt, lens, nq, nkv, hd)
+    for b in range(B):
+        L = int(lens[b])
+        pages = bt[b, : (L + page - 1) // page].long()
+        K = kc[pages].permute(1, 0, 2, 3).reshape(nkv, -1, hd)[:, :L].float()
+        V = vc[pages].permute(1, 0, 2, 3).reshape(nkv, -1, hd)[:, :L].float()
+        qq = q[b].view(nq, hd).float()
+        K = K.repeat_interleave(nq // nkv, 0)
+        V = V.repeat_interleave(nq // nkv, 0)
+        p = torch.softmax((qq.unsqueeze(1) @ K.transpose(1, 2)) / hd ** 0.5, -1)
+        ref = (p @ V).squeeze(1).reshape(-1)
+        assert rel_l2(o[b].float(), ref) < 0.01, b
+
+
+def test_ultimate_tp_mlp_single_rank(cuda_device):
+    from quantized_flash_communication_b200.model import Ultimate_TP_MLP
+    cfg = get_config("tiny")
+    mlp = Ultimate_TP_MLP(cfg, 1).to(cuda_device, torch.bfloat16)
+    x = torch.randn(2, 7, cfg.hidden_size, device=cuda_device, dtype=torch.bfloat16)
+    y = mlp(x)
+    ref = mlp.down_proj(torch.nn.functional.silu(mlp.gate_proj(x)) * mlp.up_proj(x))
+    assert rel_l2(y.float(), ref.float()) < 0.02
