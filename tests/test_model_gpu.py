@@ -24,29 +24,34 @@ def _hf(cfg, sd, dev):
 
 @pytest.mark.parametrize("name", ["tiny", "tiny-mha"])
 def test_prefill_and_decode_match_hf(cuda_device, name):
+    """Our bf16 model must be as close to an fp32 oracle as Hugging Face's bf16 model is."""
     cfg = get_config(name)
     m = LlamaTP(cfg, TPContext(device=cuda_device), cuda_device, init="full", seed=11, init_std=0.05)
-    hf = _hf(cfg, m.state_dict(), cuda_device)
+    sd = m.state_dict()
+    hf = _hf(cfg, sd, cuda_device)
+    hf32 = _hf(cfg, {k: v.float() for k, v in sd.items()}, cuda_device).float()
     B, S = 3, 100
     ids = torch.randint(0, cfg.vocab_size, (B, S), device=cuda_device)
     cache = m.new_cache(B, S + 4)
     tok, x_last = m.prefill(ids, cache, return_last_hidden=True)
     with torch.no_grad():
         out = hf(ids, output_hidden_states=True)
-    ref_h = out.hidden_states[-1][:, -1]
-    assert rel_l2(x_last.float(), ref_h.float()) < 0.03
-    ref_logits = out.logits[:, -1].float()
+        out32 = hf32(ids, output_hidden_states=True)
+    ref32 = out32.hidden_states[-1][:, -1].float()
+    err_ours = rel_l2(x_last.float(), ref32)
+    err_hf = rel_l2(out.hidden_states[-1][:, -1].float(), ref32)
+    assert err_ours <= 1.5 * err_hf + 0.01, (err_ours, err_hf)
+    ref_logits = out32.logits[:, -1].float()
     ours_logits = (x_last.float() @ m.lm_head.weight.float().T)
-    assert rel_l2(ours_logits, ref_logits) < 0.03
-    # greedy tokens agree where the top-2 margin is clear
+    assert rel_l2(ours_logits, ref_logits) <= 1.5 * rel_l2(out.logits[:, -1].float(), ref_logits) + 0.01
+    # greedy tokens agree with the fp32 oracle where its top-2 margin is clear
     top2 = ref_logits.topk(2, -1).values
     clear = (top2[:, 0] - top2[:, 1]) > 0.05 * top2[:, 0].abs().clamp_min(1)
     assert torch.equal(tok[clear], ref_logits.argmax(-1)[clear])
-    # one decode step == HF on the extended sequence
+    # one decode step == the oracle on the extended sequence
     tok2 = m.decode_step(tok, cache)
     with torch.no_grad():
-        out2 = hf(torch.cat([ids, tok.view(B, 1)], 1))
-    ref2 = out2.logits[:, -1].float()
+        ref2 = hf32(torch.cat([ids, tok.view(B, 1)], 1)).logits[:, -1].float()
     top2 = ref2.topk(2, -1).values
     clear = (top2[:, 0] - top2[:, 1]) > 0.05 * top2[:, 0].abs().clamp_min(1)
     assert torch.equal(tok2[clear], ref2.argmax(-1)[clear])

@@ -1,0 +1,151 @@
+"""Multi-GPU checks (one process per GPU, NCCL process group, CUDA-IPC peer workspaces).
+
+Skipped unless at least two GPUs are visible.  Every spin-wait in the kernels is bounded,
+and the failure test only makes a wait run out (a peer that never joins); it faults,
+traps or hangs no GPU.  NVLS is disabled for these child processes.
+"""
+import os
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import free_port
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+WORLD = min(torch.cuda.device_count(), 4) if torch.cuda.is_available() else 0
+need2 = pytest.mark.skipif(WORLD < 2, reason="needs >= 2 GPUs")
+
+
+def _inputs(world, shape, dtype, seed):
+    xs = []
+    for r in range(world):
+        g = torch.Generator().manual_seed(seed + r)
+        x = torch.randn(*shape, generator=g)
+        x.view(-1)[::1000] *= 50
+        xs.append(x.to(dtype))
+    return xs
+
+
+def _case_allreduce(rank, world):
+    from quantized_flash_communication_b200 import quantization as spec
+    from quantized_flash_communication_b200.communication import flash_all_reduce
+    from quantized_flash_communication_b200.parallel import QuantAllReduce
+    dev = torch.device("cuda", rank)
+    res = {}
+    cases = [(8, 128, "asym", (64, 4096), "two_shot"), (6, 128, "asym", (33, 4096), "two_shot"),
+             (4, 64, "sym", (16, 8192), "two_shot"), (16, 128, "asym", (128, 4096), "two_shot"),
+             (8, 128, "asym", (4, 4096), "one_shot"), (4, 128, "asym", (7, 999), "one_shot"),
+             (8, 32, "sym", (1000, 4096), "auto")]
+    for bits, gs, mode, shape, algo in cases:
+        ar = QuantAllReduce(None, dev, bits=bits, group_size=gs, quant_type=mode, algo=algo, timeout_ms=5000)
+        ok = True
+        for it in range(3):
+            xs = _inputs(world, shape, torch.bfloat16, 100 * it + bits)
+            y = ar(xs[rank].to(dev))
+            ar.check()
+            one = algo == "one_shot" or (algo == "auto" and xs[0].numel() * 2 <= 512 * 1024)
+            fn = spec.one_shot_all_reduce_ref if one else spec.two_step_all_reduce_ref
+            ref = fn(xs, bits, gs, mode, torch.float16, torch.bfloat16)
+            ok = ok and torch.equal(y.cpu(), ref)
+        res[(bits, gs, mode, shape, algo)] = ok
+    # reference-compatible API: fp16 output, host-timed latency
+    xs = _inputs(world, (8, 4096), torch.float16, 7)
+    y, ms = flash_all_reduce(xs[rank].to(dev), group_size=128, bits=8, quant_type="asym")
+    ref = spec.two_step_all_reduce_ref(xs, 8, 128, "asym", torch.float16, torch.float16)
+    res["flash_all_reduce"] = bool(torch.equal(y.cpu(), ref)) and y.dtype == torch.float16 and ms > 0
+    return res
+
+
+def _case_model(rank, world):
+    from quantized_flash_communication_b200.models.config import get_config
+    from quantized_flash_communication_b200.models.llama import LlamaTP, TPContext
+    from quantized_flash_communication_b200.quantization import rel_l2
+    dev = torch.device("cuda", rank)
+    cfg = get_config("tiny-mha")
+    ids = torch.randint(0, cfg.vocab_size, (2, 64), generator=torch.Generator().manual_seed(3)).to(dev)
+    out = {}
+    ref = LlamaTP(cfg, TPContext(device=dev, world=1), dev, init="full", seed=9)
+    _, h1 = ref.prefill(ids, return_last_hidden=True)
+    for bits in (16, 8):
+        tp = TPContext(None, dev, ar_backend="qfc", bits=bits, group_size=128)
+        m = LlamaTP(cfg, tp, dev, init="full", seed=9)
+        cache = m.new_cache(2, 80)
+        tok, h = m.prefill(ids, cache, return_last_hidden=True)
+        tok2 = m.decode_step(tok, cache)
+        gathered = [torch.empty_like(h) for _ in range(world)]
+        dist.all_gather(gathered, h)
+        out[bits] = dict(err=rel_l2(h.float(), h1.float()), same=all(torch.equal(g, h) for g in gathered),
+                         tok2_shape=tuple(tok2.shape))
+        tp.ar.check()
+    return out
+
+
+def _case_peer_never_joins(rank, world):
+    """Rank 1 skips an all-reduce: rank 0's kernel must time out and report it."""
+    from quantized_flash_communication_b200.parallel import CommTimeoutError, QuantAllReduce
+    dev = torch.device("cuda", rank)
+    ar = QuantAllReduce(None, dev, bits=8, algo="two_shot", timeout_ms=200)
+    x = torch.randn(16, 4096, device=dev, dtype=torch.bfloat16)
+    ar(x)
+    ar.check()  # one good call first
+    dist.barrier()
+    raised = None
+    if rank == 0:
+        ar(x)
+        try:
+            ar.check()
+        except CommTimeoutError as e:
+            raised = str(e)
+    torch.cuda.synchronize()
+    dist.barrier()
+    return raised
+
+
+def _worker(rank, world, port, case, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        results[rank] = globals()[case](rank, world)
+    finally:
+        from quantized_flash_communication_b200.communication import reset_communicators
+        reset_communicators()
+        dist.destroy_process_group()
+
+
+def _run(case, world=WORLD):
+    mgr = mp.Manager()
+    results = mgr.dict()
+    mp.spawn(_worker, args=(world, free_port(), case, results), nprocs=world, join=True)
+    return dict(results)
+
+
+@need2
+def test_fused_allreduce_matches_oracle_on_every_rank():
+    res = _run("_case_allreduce")
+    for rank, r in res.items():
+        for k, ok in r.items():
+            assert ok, (rank, k)
+
+
+@need2
+def test_tp_model_matches_tp1():
+    res = _run("_case_model")
+    for rank, r in res.items():
+        assert r[16]["err"] < 0.02, r
+        assert r[8]["err"] < 0.08, r
+        assert r[16]["same"] and r[8]["same"]
+
+
+@need2
+def test_peer_that_never_joins_times_out_cleanly():
+    res = _run("_case_peer_never_joins", world=2)
+    assert res[0] is not None and "timed out" in res[0]
+    assert res[1] is None
