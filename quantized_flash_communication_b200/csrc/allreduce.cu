@@ -162,26 +162,102 @@ QFC_DEV void decode8(const Enc8& e, int meta_fp32, float (&d)[8]) {
   }
 }
 
-// Read one lane's 8 elements back from a slot in local memory (L2, bypassing L1: the
-// bytes were written by another GPU).
+// Raw 8 elements of the input: one 16-byte vector for 16-bit types, two for fp32.
+// Elements at or beyond n read as zero (the zero padding of the last chunk).
+template <typename T>
+struct Raw8 {
+  uint4 a, b;
+};
+template <typename T>
+QFC_DEV Raw8<T> load_raw8(const T* base, int64_t idx, int64_t n) {
+  Raw8<T> r;
+  r.a = make_uint4(0, 0, 0, 0);
+  r.b = make_uint4(0, 0, 0, 0);
+  if (idx + 8 <= n) {
+    r.a = *reinterpret_cast<const uint4*>(base + idx);
+    if constexpr (sizeof(T) == 4) r.b = *(reinterpret_cast<const uint4*>(base + idx) + 1);
+  } else {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (idx + i < n) ? to_f32(base[idx + i]) : 0.f;
+    if constexpr (sizeof(T) == 4) {
+      r.a = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+      r.b = make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]), __float_as_uint(v[7]));
+    } else {
+      r.a = Vec8IO<T>::pack(v);
+    }
+  }
+  return r;
+}
+template <typename T>
+QFC_DEV void raw8_to_f32(const Raw8<T>& r, float (&v)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    v[0] = __uint_as_float(r.a.x); v[1] = __uint_as_float(r.a.y);
+    v[2] = __uint_as_float(r.a.z); v[3] = __uint_as_float(r.a.w);
+    v[4] = __uint_as_float(r.b.x); v[5] = __uint_as_float(r.b.y);
+    v[6] = __uint_as_float(r.b.z); v[7] = __uint_as_float(r.b.w);
+  } else {
+    const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) unpack_bf16x2(w[i], v[2 * i], v[2 * i + 1]);
+      else unpack_f16x2(w[i], v[2 * i], v[2 * i + 1]);
+    }
+  }
+}
+
+// One lane's 8 elements as they sit in a slot: payload words + the group's metadata.
+struct Wire8 {
+  uint4 a, b;
+  float s, z;
+};
+
+// Read a lane's wire data from a slot in local memory (L2, bypassing L1: the bytes were
+// written by another GPU).  Separate from decoding so that a warp can put the loads of
+// all W slots in flight before it uses any of them.
 template <int P, typename WT>
-QFC_DEV void load8(const char* slot, const char* meta, int64_t loc, int gs, int meta_fp32, float (&d)[8]) {
+QFC_DEV Wire8 load_wire(const char* slot, const char* meta, int64_t loc, int gs, int meta_fp32) {
+  Wire8 w;
+  w.b = make_uint4(0, 0, 0, 0);
+  w.s = 1.f;
+  w.z = 0.f;
   if constexpr (P == 16) {
-    Vec8IO<WT>::load_cg(reinterpret_cast<const WT*>(slot) + loc, d);
+    const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const WT*>(slot) + loc);
+    w.a = __ldcg(p);
+    if constexpr (sizeof(WT) == 4) w.b = __ldcg(p + 1);
   } else {
     const int64_t g = loc / gs;
-    float s, z;
     if (meta_fp32) {
       const float2 m = __ldcg(reinterpret_cast<const float2*>(meta + g * 8));
-      s = m.x;
-      z = m.y;
+      w.s = m.x;
+      w.z = m.y;
     } else {
       const uint32_t m = __ldcg(reinterpret_cast<const unsigned int*>(meta + g * 4));
-      unpack_f16x2(m, s, z);
+      w.s = __uint_as_float(m);  // unpacked in decode_wire
     }
+    if constexpr (P == 8) {
+      const uint2 u = __ldcg(reinterpret_cast<const uint2*>(slot + loc));
+      w.a = make_uint4(u.x, u.y, 0, 0);
+    } else {
+      w.a = make_uint4(__ldcg(reinterpret_cast<const unsigned int*>(slot + (loc >> 1))), 0, 0, 0);
+    }
+  }
+  return w;
+}
+
+template <int P, typename WT>
+QFC_DEV void decode_wire(const Wire8& w, int meta_fp32, float (&d)[8]) {
+  if constexpr (P == 16) {
+    Raw8<WT> r;
+    r.a = w.a;
+    r.b = w.b;
+    raw8_to_f32<WT>(r, d);
+  } else {
+    float s = w.s, z = w.z;
+    if (!meta_fp32) unpack_f16x2(__float_as_uint(w.s), s, z);
     uint32_t c[8];
-    if constexpr (P == 8) u2_to_codes8(__ldcg(reinterpret_cast<const uint2*>(slot + loc)), c);
-    else int4_to_codes8(__ldcg(reinterpret_cast<const unsigned int*>(slot + (loc >> 1))), c);
+    if constexpr (P == 8) u2_to_codes8(make_uint2(w.a.x, w.a.y), c);
+    else int4_to_codes8(w.a.x, c);
 #pragma unroll
     for (int i = 0; i < 8; ++i) d[i] = dq(c[i], z, s);
   }
@@ -229,17 +305,28 @@ __global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ A
   const int64_t u0 = (int64_t)b * wpb + warp;
 
   // Phase 1: quantize every chunk's units of this block, push to the chunk's owner.
+  // All W chunk loads of a unit are issued before any of them is used.
   for (int64_t u = u0; u < units; u += ustride) {
     const int64_t loc = (u << 8) + lane * 8;
-#pragma unroll 1
-    for (int jj = 1; jj <= W; ++jj) {
-      const int j = (rank + jj) % W;  // peers staggered, own chunk last
-      if (j == rank && !p.quantize_local) continue;
-      float v[8];
-      load8_guard(in, (int64_t)j * C + loc, p.n, v);
-      const Enc8 en = encode8<P1, InT>(v, lpg, p.sym);
-      char* slot = p.base[j] + p.rs_off + (int64_t)rank * p.slot1;
-      store8<P1, InT>(slot, slot + p.pay1, loc, en, leader, p.gs, p.meta_fp32);
+    Raw8<InT> raw[kMaxRanks];
+#pragma unroll
+    for (int jj = 0; jj < kMaxRanks; ++jj) {
+      if (jj < W) {
+        const int j = (rank + 1 + jj) % W;  // peers staggered, own chunk last
+        raw[jj] = load_raw8(in, (int64_t)j * C + loc, p.n);
+      }
+    }
+#pragma unroll
+    for (int jj = 0; jj < kMaxRanks; ++jj) {
+      if (jj < W) {
+        const int j = (rank + 1 + jj) % W;
+        if (j == rank && !p.quantize_local) continue;
+        float v[8];
+        raw8_to_f32(raw[jj], v);
+        const Enc8 en = encode8<P1, InT>(v, lpg, p.sym);
+        char* slot = p.base[j] + p.rs_off + (int64_t)rank * p.slot1;
+        store8<P1, InT>(slot, slot + p.pay1, loc, en, leader, p.gs, p.meta_fp32);
+      }
     }
   }
   __syncthreads();
@@ -249,27 +336,35 @@ __global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ A
   // Phase 2: reduce the own chunk, requantize, push to every peer, write own output.
   for (int64_t u = u0; u < units; u += ustride) {
     const int64_t loc = (u << 8) + lane * 8;
+    Wire8 wv[kMaxRanks];
+#pragma unroll
+    for (int s = 0; s < kMaxRanks; ++s) {
+      if (s < W && !(s == rank && !p.quantize_local)) {
+        const char* slot = my + p.rs_off + (int64_t)s * p.slot1;
+        wv[s] = load_wire<P1, InT>(slot, slot + p.pay1, loc, p.gs, p.meta_fp32);
+      }
+    }
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-#pragma unroll 1
-    for (int s = 0; s < W; ++s) {
-      float d[8];
-      if (s == rank && !p.quantize_local) {
-        load8_guard(in, (int64_t)rank * C + loc, p.n, d);
-      } else {
-        const char* slot = my + p.rs_off + (int64_t)s * p.slot1;
-        load8<P1, InT>(slot, slot + p.pay1, loc, p.gs, p.meta_fp32, d);
-      }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], d[i]);
+    for (int s = 0; s < kMaxRanks; ++s) {
+      if (s < W) {
+        float d[8];
+        if (s == rank && !p.quantize_local) load8_guard(in, (int64_t)rank * C + loc, p.n, d);
+        else decode_wire<P1, InT>(wv[s], p.meta_fp32, d);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], d[i]);
+      }
     }
     const Enc8 en = encode8<P2, InT>(acc, lpg, p.sym);
-#pragma unroll 1
-    for (int jj = 1; jj < W; ++jj) {
-      const int j = (rank + jj) % W;
-      char* slot = p.base[j] + p.ag_off + (int64_t)rank * p.slot2;
-      store8<P2, InT>(slot, slot + p.pay2, loc, en, leader, p.gs, p.meta_fp32);
+#pragma unroll
+    for (int jj = 1; jj < kMaxRanks; ++jj) {
+      if (jj < W) {
+        const int j = (rank + jj) % W;
+        char* slot = p.base[j] + p.ag_off + (int64_t)rank * p.slot2;
+        store8<P2, InT>(slot, slot + p.pay2, loc, en, leader, p.gs, p.meta_fp32);
+      }
     }
     float o[8];
     decode8<P2, InT>(en, p.meta_fp32, o);
@@ -283,13 +378,23 @@ __global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ A
   // Phase 3: dequantize the gathered chunks of the other ranks.
   for (int64_t u = u0; u < units; u += ustride) {
     const int64_t loc = (u << 8) + lane * 8;
-#pragma unroll 1
-    for (int jj = 1; jj < W; ++jj) {
-      const int j = (rank + jj) % W;
-      const char* slot = my + p.ag_off + (int64_t)j * p.slot2;
-      float d[8];
-      load8<P2, InT>(slot, slot + p.pay2, loc, p.gs, p.meta_fp32, d);
-      store8_guard(out, (int64_t)j * C + loc, p.n, d);
+    Wire8 wv[kMaxRanks];
+#pragma unroll
+    for (int jj = 1; jj < kMaxRanks; ++jj) {
+      if (jj < W) {
+        const int j = (rank + jj) % W;
+        const char* slot = my + p.ag_off + (int64_t)j * p.slot2;
+        wv[jj] = load_wire<P2, InT>(slot, slot + p.pay2, loc, p.gs, p.meta_fp32);
+      }
+    }
+#pragma unroll
+    for (int jj = 1; jj < kMaxRanks; ++jj) {
+      if (jj < W) {
+        const int j = (rank + jj) % W;
+        float d[8];
+        decode_wire<P2, InT>(wv[jj], p.meta_fp32, d);
+        store8_guard(out, (int64_t)j * C + loc, p.n, d);
+      }
     }
   }
   if (threadIdx.x == 0) *ep = e;
@@ -327,11 +432,13 @@ __global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ A
     float v[8];
     load8_guard(in, loc, p.n, v);
     const Enc8 en = encode8<P, InT>(v, lpg, p.sym);
-#pragma unroll 1
-    for (int jj = 1; jj < W; ++jj) {
-      const int j = (rank + jj) % W;
-      char* slot = p.base[j] + region + (int64_t)rank * p.slot1;
-      store8<P, InT>(slot, slot + p.pay1, loc, en, leader, p.gs, p.meta_fp32);
+#pragma unroll
+    for (int jj = 1; jj < kMaxRanks; ++jj) {
+      if (jj < W) {
+        const int j = (rank + jj) % W;
+        char* slot = p.base[j] + region + (int64_t)rank * p.slot1;
+        store8<P, InT>(slot, slot + p.pay1, loc, en, leader, p.gs, p.meta_fp32);
+      }
     }
   }
   __syncthreads();
@@ -341,28 +448,36 @@ __global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ A
 
   for (int64_t u = u0; u < units; u += ustride) {
     const int64_t loc = (u << 8) + lane * 8;
+    Wire8 wv[kMaxRanks];
+#pragma unroll
+    for (int s = 0; s < kMaxRanks; ++s) {
+      if (s < W && s != rank) {
+        const char* slot = my + region + (int64_t)s * p.slot1;
+        wv[s] = load_wire<P, InT>(slot, slot + p.pay1, loc, p.gs, p.meta_fp32);
+      }
+    }
+    float own[8];
+    load8_guard(in, loc, p.n, own);
+    if (p.quantize_local) {
+      const Enc8 en = encode8<P, InT>(own, lpg, p.sym);
+      decode8<P, InT>(en, p.meta_fp32, own);
+    }
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-#pragma unroll 1
-    for (int s = 0; s < W; ++s) {
-      float d[8];
-      if (s == rank) {
-        float v[8];
-        load8_guard(in, loc, p.n, v);
-        if (p.quantize_local) {
-          const Enc8 en = encode8<P, InT>(v, lpg, p.sym);
-          decode8<P, InT>(en, p.meta_fp32, d);
+#pragma unroll
+    for (int s = 0; s < kMaxRanks; ++s) {
+      if (s < W) {
+        float d[8];
+        if (s == rank) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) d[i] = own[i];
         } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) d[i] = v[i];
+          decode_wire<P, InT>(wv[s], p.meta_fp32, d);
         }
-      } else {
-        const char* slot = my + region + (int64_t)s * p.slot1;
-        load8<P, InT>(slot, slot + p.pay1, loc, p.gs, p.meta_fp32, d);
-      }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], d[i]);
+        for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], d[i]);
+      }
     }
     store8_guard(out, loc, p.n, acc);
   }
