@@ -67,51 +67,69 @@ struct Enc8 {
   float s, z;
 };
 
+// Quantize 8 values given their group's (min, max).
 template <int P>
-QFC_DEV void quantize8(const float (&v)[8], int lpg, bool sym, uint32_t (&c)[8], float& s, float& z) {
-  float mn = v[0], mx = v[0];
-#pragma unroll
-  for (int i = 1; i < 8; ++i) {
-    mn = fminf(mn, v[i]);
-    mx = fmaxf(mx, v[i]);
-  }
-  for (int off = lpg >> 1; off > 0; off >>= 1) {
-    mn = fminf(mn, __shfl_xor_sync(QFC_FULL_MASK, mn, off));
-    mx = fmaxf(mx, __shfl_xor_sync(QFC_FULL_MASK, mx, off));
-  }
-  float inv;
-  if (sym) QMath<P, true>::params(mn, mx, s, inv, z);
-  else QMath<P, false>::params(mn, mx, s, inv, z);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) c[i] = QMath<P, false>::code(v[i], inv, z);
-}
-
-template <int P, typename WT>
-QFC_DEV Enc8 encode8(const float (&v)[8], int lpg, bool sym) {
+QFC_DEV Enc8 encode_stats(const float (&v)[8], float mn, float mx, bool sym) {
   Enc8 e;
   e.a = make_uint4(0, 0, 0, 0);
   e.b = make_uint4(0, 0, 0, 0);
-  e.s = 1.f;
-  e.z = 0.f;
+  float inv;
+  if (sym) QMath<P, true>::params(mn, mx, e.s, inv, e.z);
+  else QMath<P, false>::params(mn, mx, e.s, inv, e.z);
+  uint32_t m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = QMath<P, false>::codebits(v[i], inv, e.z);
+  if constexpr (P == 8) {
+    const uint2 u = codebits8_to_u2(m);
+    e.a.x = u.x;
+    e.a.y = u.y;
+  } else {
+    e.a.x = codebits8_to_int4(m);
+  }
+  return e;
+}
+
+// Wire form of 8 fp32 values (group statistics from the values themselves).
+template <int P, typename WT>
+QFC_DEV Enc8 encode8(const float (&v)[8], int lpg, bool sym) {
   if constexpr (P == 16) {
+    Enc8 e;
+    e.b = make_uint4(0, 0, 0, 0);
+    e.s = 1.f;
+    e.z = 0.f;
     if constexpr (sizeof(WT) == 2) {
       e.a = Vec8IO<WT>::pack(v);
     } else {
       e.a = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
       e.b = make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]), __float_as_uint(v[7]));
     }
+    return e;
   } else {
-    uint32_t c[8];
-    quantize8<P>(v, lpg, sym, c, e.s, e.z);
-    if constexpr (P == 8) {
-      const uint2 u = codes8_to_u2(c);
-      e.a.x = u.x;
-      e.a.y = u.y;
-    } else {
-      e.a.x = codes8_to_int4(c);
-    }
+    float mn, mx;
+    group_minmax_f32(v, lpg, mn, mx);
+    return encode_stats<P>(v, mn, mx, sym);
   }
-  return e;
+}
+
+// Wire form of 8 raw input elements; 16-bit inputs reduce their group statistics on the
+// packed values.  v receives the fp32 values.
+template <int P, typename WT>
+QFC_DEV Enc8 encode_raw(const Raw8<WT>& r, int lpg, bool sym, float (&v)[8]) {
+  raw8_to_f32(r, v);
+  if constexpr (P == 16) {
+    Enc8 e;
+    e.a = r.a;
+    e.b = r.b;
+    e.s = 1.f;
+    e.z = 0.f;
+    return e;
+  } else if constexpr (sizeof(WT) == 2) {
+    float mn, mx;
+    group_minmax16<WT>(r.a, lpg, mn, mx);
+    return encode_stats<P>(v, mn, mx, sym);
+  } else {
+    return encode8<P, WT>(v, lpg, sym);
+  }
 }
 
 template <int P, typename WT>
@@ -153,56 +171,9 @@ QFC_DEV void decode8(const Enc8& e, int meta_fp32, float (&d)[8]) {
       d[6] = __uint_as_float(e.b.z); d[7] = __uint_as_float(e.b.w);
     }
   } else {
-    uint32_t c[8];
-    if constexpr (P == 8) u2_to_codes8(make_uint2(e.a.x, e.a.y), c);
-    else int4_to_codes8(e.a.x, c);
     const float ss = meta_fp32 ? e.s : __half2float(__float2half_rn(e.s));
-#pragma unroll
-    for (int i = 0; i < 8; ++i) d[i] = dq(c[i], e.z, ss);
-  }
-}
-
-// Raw 8 elements of the input: one 16-byte vector for 16-bit types, two for fp32.
-// Elements at or beyond n read as zero (the zero padding of the last chunk).
-template <typename T>
-struct Raw8 {
-  uint4 a, b;
-};
-template <typename T>
-QFC_DEV Raw8<T> load_raw8(const T* base, int64_t idx, int64_t n) {
-  Raw8<T> r;
-  r.a = make_uint4(0, 0, 0, 0);
-  r.b = make_uint4(0, 0, 0, 0);
-  if (idx + 8 <= n) {
-    r.a = *reinterpret_cast<const uint4*>(base + idx);
-    if constexpr (sizeof(T) == 4) r.b = *(reinterpret_cast<const uint4*>(base + idx) + 1);
-  } else {
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = (idx + i < n) ? to_f32(base[idx + i]) : 0.f;
-    if constexpr (sizeof(T) == 4) {
-      r.a = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
-      r.b = make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]), __float_as_uint(v[7]));
-    } else {
-      r.a = Vec8IO<T>::pack(v);
-    }
-  }
-  return r;
-}
-template <typename T>
-QFC_DEV void raw8_to_f32(const Raw8<T>& r, float (&v)[8]) {
-  if constexpr (sizeof(T) == 4) {
-    v[0] = __uint_as_float(r.a.x); v[1] = __uint_as_float(r.a.y);
-    v[2] = __uint_as_float(r.a.z); v[3] = __uint_as_float(r.a.w);
-    v[4] = __uint_as_float(r.b.x); v[5] = __uint_as_float(r.b.y);
-    v[6] = __uint_as_float(r.b.z); v[7] = __uint_as_float(r.b.w);
-  } else {
-    const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if constexpr (std::is_same<T, __nv_bfloat16>::value) unpack_bf16x2(w[i], v[2 * i], v[2 * i + 1]);
-      else unpack_f16x2(w[i], v[2 * i], v[2 * i + 1]);
-    }
+    if constexpr (P == 8) dq_u2(make_uint2(e.a.x, e.a.y), e.z, ss, d);
+    else dq_u2(int4_to_u2(e.a.x), e.z, ss, d);
   }
 }
 
@@ -255,11 +226,8 @@ QFC_DEV void decode_wire(const Wire8& w, int meta_fp32, float (&d)[8]) {
   } else {
     float s = w.s, z = w.z;
     if (!meta_fp32) unpack_f16x2(__float_as_uint(w.s), s, z);
-    uint32_t c[8];
-    if constexpr (P == 8) u2_to_codes8(make_uint2(w.a.x, w.a.y), c);
-    else int4_to_codes8(w.a.x, c);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) d[i] = dq(c[i], z, s);
+    if constexpr (P == 8) dq_u2(make_uint2(w.a.x, w.a.y), z, s, d);
+    else dq_u2(int4_to_u2(w.a.x), z, s, d);
   }
 }
 
@@ -322,8 +290,7 @@ __global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ A
         const int j = (rank + 1 + jj) % W;
         if (j == rank && !p.quantize_local) continue;
         float v[8];
-        raw8_to_f32(raw[jj], v);
-        const Enc8 en = encode8<P1, InT>(v, lpg, p.sym);
+        const Enc8 en = encode_raw<P1, InT>(raw[jj], lpg, p.sym, v);
         char* slot = p.base[j] + p.rs_off + (int64_t)rank * p.slot1;
         store8<P1, InT>(slot, slot + p.pay1, loc, en, leader, p.gs, p.meta_fp32);
       }
@@ -430,8 +397,7 @@ __global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ A
   for (int64_t u = u0; u < units; u += ustride) {
     const int64_t loc = (u << 8) + lane * 8;
     float v[8];
-    load8_guard(in, loc, p.n, v);
-    const Enc8 en = encode8<P, InT>(v, lpg, p.sym);
+    const Enc8 en = encode_raw<P, InT>(load_raw8(in, loc, p.n), lpg, p.sym, v);
 #pragma unroll
     for (int jj = 1; jj < kMaxRanks; ++jj) {
       if (jj < W) {
@@ -457,11 +423,8 @@ __global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ A
       }
     }
     float own[8];
-    load8_guard(in, loc, p.n, own);
-    if (p.quantize_local) {
-      const Enc8 en = encode8<P, InT>(own, lpg, p.sym);
-      decode8<P, InT>(en, p.meta_fp32, own);
-    }
+    const Enc8 en_own = encode_raw<P, InT>(load_raw8(in, loc, p.n), lpg, p.sym, own);
+    if (p.quantize_local) decode8<P, InT>(en_own, p.meta_fp32, own);
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;

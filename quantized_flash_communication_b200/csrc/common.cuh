@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "status.h"
 
 #define QFC_DEV __device__ __forceinline__
@@ -146,40 +148,67 @@ QFC_DEV void store8_guard(T* base, int64_t idx, int64_t n, const float (&v)[8]) 
 // ------------------------------------------------------------------------------------
 // Quantizer arithmetic (must stay identical to quantization.quantize_groups)
 // ------------------------------------------------------------------------------------
-// Round half away from zero.
-QFC_DEV float rhaz(float v) { return roundf(v); }
+// Round half away from zero, exactly, without the libm routine: for any finite v,
+// trunc(|v| + 0.49999997f) == floor(|v| + 0.5).  0.49999997f is the largest float below
+// 0.5.  Proof sketch: if frac(|v|) >= 0.5 the true sum is >= k + 0.99999997 and rounds to
+// >= k + 1 in the result's binade (half an ulp there is >= 2^-25); if frac(|v|) < 0.5 the
+// true sum is <= k + 1 - ulp(v) - 2^-25, which rounds to below k + 1.  (With 0.5 itself,
+// v = 0.49999997 would round up to 1.)  Tested exhaustively on ties and their
+// neighbours against the oracle.
+QFC_DEV float rhaz(float v) { return copysignf(truncf(fabsf(v) + 0.49999997f), v); }
+
+constexpr float kMagic = 8388608.f;  // 2^23: (2^23 + c) holds the integer c in its low mantissa bits
 
 template <int BITS, bool SYM>
 struct QMath {
   static constexpr float QMAX = float((1 << BITS) - 1);
-  // Group statistics -> (scale, 1/scale, zero point), all fp32.
+  // Group statistics -> (scale, 1/scale, zero point), all fp32, IEEE-rounded.
   static QFC_DEV void params(float mn, float mx, float& s, float& inv, float& z) {
     if (SYM) {
       const float a = fmaxf(-mn, mx);  // == max |x| over the group
-      s = a / (QMAX * 0.5f);
+      s = __fdiv_rn(a, QMAX * 0.5f);
       if (s < 1e-9f) s = 1.f;
-      inv = 1.f / s;
+      inv = __frcp_rn(s);
       z = (QMAX + 1.f) * 0.5f;
     } else {
-      s = (mx - mn) / QMAX;
+      s = __fdiv_rn(mx - mn, QMAX);
       if (s < 1e-9f) s = 1.f;
-      inv = 1.f / s;
+      inv = __frcp_rn(s);
       z = fminf(fmaxf(rhaz(-mn * inv), 0.f), QMAX);
     }
   }
-  static QFC_DEV uint32_t code(float x, float inv, float z) {
-    return (uint32_t)fminf(fmaxf(rhaz(x * inv) + z, 0.f), QMAX);
+  // The code of x as the bit pattern of the float 2^23 + code (code in the low byte).
+  static QFC_DEV uint32_t codebits(float x, float inv, float z) {
+    return __float_as_uint(fminf(fmaxf(rhaz(x * inv) + z, 0.f), QMAX) + kMagic);
   }
+  static QFC_DEV uint32_t code(float x, float inv, float z) { return codebits(x, inv, z) & 0xffu; }
 };
 
-// Dequantize one code.  __fmul_rn keeps the product from being fused into a following
-// add, so that sums match the oracle's separately rounded (q - z) * s terms.
-QFC_DEV float dq(uint32_t c, float z, float s) { return __fmul_rn((float)c - z, s); }
+// Dequantize one code: (c - z) * s.  Both subtractions below are exact (integers < 2^24),
+// so this equals the oracle's (float(c) - z) * s; __fmul_rn keeps the product from being
+// fused into a following add.
+QFC_DEV float dq(uint32_t c, float z, float s) {
+  return __fmul_rn(__uint_as_float(0x4b000000u | c) - (kMagic + z), s);
+}
+// Same, with zb = 2^23 + z precomputed and the code already in magic-float form.
+QFC_DEV float dq_bits(uint32_t cbits, float zb, float s) { return __fmul_rn(__uint_as_float(cbits) - zb, s); }
 
-// 8 byte codes (element order) <-> uint2
+// Byte i of w as the magic float bits 0x4B0000cc.
+template <int I>
+QFC_DEV uint32_t byte_magic(uint32_t w) {
+  return __byte_perm(w, 0x4b000000u, 0x7440 | I);
+}
+
+// 8 byte codes <-> uint2 (element order)
 QFC_DEV uint2 codes8_to_u2(const uint32_t (&c)[8]) {
   return make_uint2(c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24),
                     c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24));
+}
+// From magic-float code bits (code in byte 0 of each word).
+QFC_DEV uint2 codebits8_to_u2(const uint32_t (&m)[8]) {
+  const uint32_t a = __byte_perm(m[0], m[1], 0x0040), b = __byte_perm(m[2], m[3], 0x0040);
+  const uint32_t c = __byte_perm(m[4], m[5], 0x0040), d = __byte_perm(m[6], m[7], 0x0040);
+  return make_uint2(__byte_perm(a, b, 0x5410), __byte_perm(c, d, 0x5410));
 }
 QFC_DEV void u2_to_codes8(uint2 u, uint32_t (&c)[8]) {
 #pragma unroll
@@ -187,6 +216,18 @@ QFC_DEV void u2_to_codes8(uint2 u, uint32_t (&c)[8]) {
     c[i] = (u.x >> (8 * i)) & 0xffu;
     c[4 + i] = (u.y >> (8 * i)) & 0xffu;
   }
+}
+// uint2 of byte codes -> 8 dequantized values.
+QFC_DEV void dq_u2(uint2 u, float z, float s, float (&d)[8]) {
+  const float zb = kMagic + z;
+  d[0] = dq_bits(byte_magic<0>(u.x), zb, s);
+  d[1] = dq_bits(byte_magic<1>(u.x), zb, s);
+  d[2] = dq_bits(byte_magic<2>(u.x), zb, s);
+  d[3] = dq_bits(byte_magic<3>(u.x), zb, s);
+  d[4] = dq_bits(byte_magic<0>(u.y), zb, s);
+  d[5] = dq_bits(byte_magic<1>(u.y), zb, s);
+  d[6] = dq_bits(byte_magic<2>(u.y), zb, s);
+  d[7] = dq_bits(byte_magic<3>(u.y), zb, s);
 }
 
 // INT4: 8 codes -> one word; nibble k (from the LSB) holds element {0,2,4,6,1,3,5,7}[k].
@@ -207,6 +248,96 @@ QFC_DEV void int4_to_codes8(uint32_t w, uint32_t (&c)[8]) {
   const uint32_t b = (w >> 4) & 0x0f0f0f0fu;   // bytes: c2 c6 c3 c7
   uint2 u = make_uint2(__byte_perm(a, b, 0x6420), __byte_perm(a, b, 0x7531));
   u2_to_codes8(u, c);
+}
+// INT4 word -> uint2 of byte codes in element order.
+QFC_DEV uint2 int4_to_u2(uint32_t w) {
+  const uint32_t a = w & 0x0f0f0f0fu, b = (w >> 4) & 0x0f0f0f0fu;
+  return make_uint2(__byte_perm(a, b, 0x6420), __byte_perm(a, b, 0x7531));
+}
+// 8 magic-float code words (codes <= 15) -> INT4 word.
+QFC_DEV uint32_t codebits8_to_int4(const uint32_t (&m)[8]) {
+  const uint2 u = codebits8_to_u2(m);
+  return pack_nibbles(u.x, u.y);
+}
+
+// ------------------------------------------------------------------------------------
+// Raw 8-element vectors and group statistics
+// ------------------------------------------------------------------------------------
+// Raw 8 elements: one 16-byte vector for 16-bit types, two for fp32.  Elements at or
+// beyond n read as zero.
+template <typename T>
+struct Raw8 {
+  uint4 a, b;
+};
+template <typename T>
+QFC_DEV Raw8<T> load_raw8(const T* base, int64_t idx, int64_t n) {
+  Raw8<T> r;
+  r.a = make_uint4(0, 0, 0, 0);
+  r.b = make_uint4(0, 0, 0, 0);
+  if (idx + 8 <= n) {
+    r.a = *reinterpret_cast<const uint4*>(base + idx);
+    if constexpr (sizeof(T) == 4) r.b = *(reinterpret_cast<const uint4*>(base + idx) + 1);
+  } else {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (idx + i < n) ? to_f32(base[idx + i]) : 0.f;
+    if constexpr (sizeof(T) == 4) {
+      r.a = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+      r.b = make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]), __float_as_uint(v[7]));
+    } else {
+      r.a = Vec8IO<T>::pack(v);
+    }
+  }
+  return r;
+}
+template <typename T>
+QFC_DEV void raw8_to_f32(const Raw8<T>& r, float (&v)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    v[0] = __uint_as_float(r.a.x); v[1] = __uint_as_float(r.a.y);
+    v[2] = __uint_as_float(r.a.z); v[3] = __uint_as_float(r.a.w);
+    v[4] = __uint_as_float(r.b.x); v[5] = __uint_as_float(r.b.y);
+    v[6] = __uint_as_float(r.b.z); v[7] = __uint_as_float(r.b.w);
+  } else {
+    const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) unpack_bf16x2(w[i], v[2 * i], v[2 * i + 1]);
+      else unpack_f16x2(w[i], v[2 * i], v[2 * i + 1]);
+    }
+  }
+}
+
+// Min and max of a group spread over lpg consecutive lanes (8 fp32 values per lane).
+QFC_DEV void group_minmax_f32(const float (&v)[8], int lpg, float& mn, float& mx) {
+  mn = fminf(fminf(fminf(v[0], v[1]), fminf(v[2], v[3])), fminf(fminf(v[4], v[5]), fminf(v[6], v[7])));
+  mx = fmaxf(fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])), fmaxf(fmaxf(v[4], v[5]), fmaxf(v[6], v[7])));
+  for (int off = lpg >> 1; off > 0; off >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(QFC_FULL_MASK, mn, off));
+    mx = fmaxf(mx, __shfl_xor_sync(QFC_FULL_MASK, mx, off));
+  }
+}
+
+// Same for 16-bit inputs, on the packed values: the pair (-min, max) travels as one
+// bf16x2 / half2 word, so each reduction level is one shuffle and one packed max.
+// Negation and min / max are exact, so the result equals the fp32 computation.
+template <typename T>
+QFC_DEV void group_minmax16(const uint4& r, int lpg, float& mn, float& mx) {
+  using T2 = typename std::conditional<std::is_same<T, __nv_bfloat16>::value, __nv_bfloat162, __half2>::type;
+  auto as2 = [](uint32_t u) { return *reinterpret_cast<T2*>(&u); };
+  auto bits = [](T2 x) { return *reinterpret_cast<uint32_t*>(&x); };
+  const T2 hi = __hmax2(__hmax2(as2(r.x), as2(r.y)), __hmax2(as2(r.z), as2(r.w)));
+  const T2 lo = __hmin2(__hmin2(as2(r.x), as2(r.y)), __hmin2(as2(r.z), as2(r.w)));
+  const uint32_t nlo = bits(lo) ^ 0x80008000u;              // (-min_even, -min_odd)
+  const uint32_t q1 = __byte_perm(nlo, bits(hi), 0x7610);   // (-min_even, max_odd)
+  const uint32_t q2 = __byte_perm(nlo, bits(hi), 0x5432);   // (-min_odd,  max_even)
+  uint32_t p = bits(__hmax2(as2(q1), as2(q2)));             // (-min, max)
+  for (int off = lpg >> 1; off > 0; off >>= 1)
+    p = bits(__hmax2(as2(p), as2(__shfl_xor_sync(QFC_FULL_MASK, p, off))));
+  float a, b;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) unpack_bf16x2(p, a, b);
+  else unpack_f16x2(p, a, b);
+  mn = -a;
+  mx = b;
 }
 
 // ------------------------------------------------------------------------------------

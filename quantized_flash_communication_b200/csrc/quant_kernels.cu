@@ -46,28 +46,23 @@ quantize_kernel(const T* __restrict__ x, uint8_t* __restrict__ q, ST* __restrict
     const int64_t n_units = (n + 255) / 256;
     for (int64_t u = warp; u < n_units; u += nwarps) {
       const int64_t idx = u * 256 + lane * 8;
+      const Raw8<T> raw = load_raw8(x, idx, n);
       float v[8];
-      load8_guard(x, idx, n, v);
-      float mn = v[0], mx = v[0];
-#pragma unroll
-      for (int i = 1; i < 8; ++i) {
-        mn = fminf(mn, v[i]);
-        mx = fmaxf(mx, v[i]);
-      }
-      for (int off = lpg >> 1; off > 0; off >>= 1) {
-        mn = fminf(mn, __shfl_xor_sync(QFC_FULL_MASK, mn, off));
-        mx = fmaxf(mx, __shfl_xor_sync(QFC_FULL_MASK, mx, off));
-      }
+      raw8_to_f32(raw, v);
+      float mn, mx;
+      if constexpr (sizeof(T) == 2) group_minmax16<T>(raw.a, lpg, mn, mx);
+      else group_minmax_f32(v, lpg, mn, mx);
       float s, inv, z;
       QM::params(mn, mx, s, inv, z);
-      uint32_t c[8];
+      uint32_t m[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) c[i] = QM::code(v[i], inv, z);
+      for (int i = 0; i < 8; ++i) m[i] = QM::codebits(v[i], inv, z);
+      const uint2 packed = codebits8_to_u2(m);
       if (idx + 8 <= n) {
-        *reinterpret_cast<uint2*>(q + idx) = codes8_to_u2(c);
+        *reinterpret_cast<uint2*>(q + idx) = packed;
       } else {
         for (int i = 0; i < 8; ++i)
-          if (idx + i < n) q[idx + i] = (uint8_t)c[i];
+          if (idx + i < n) q[idx + i] = (uint8_t)(m[i] & 0xffu);
       }
       if ((lane & (lpg - 1)) == 0 && idx < n) {
         const int64_t g = idx / gs;
@@ -152,11 +147,15 @@ dequantize_kernel(const QT* __restrict__ q, const ST* __restrict__ s, const __ha
     const int64_t g = idx / gs;
     const float sc = to_f32(s[g]);
     const float zz = __half2float(z[g]);
-    uint32_t c[8];
-    CodeLoad<QT>::load(q, idx, n, c);
     float v[8];
+    if (std::is_same<QT, uint8_t>::value && idx + 8 <= n) {
+      dq_u2(*reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(q) + idx), zz, sc, v);
+    } else {
+      uint32_t c[8];
+      CodeLoad<QT>::load(q, idx, n, c);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = dq(c[i], zz, sc);
+      for (int i = 0; i < 8; ++i) v[i] = dq(c[i], zz, sc);
+    }
     store8_guard(out, idx, n, v);
   }
 }

@@ -98,3 +98,24 @@ def test_compat_api_shapes_cpu():
     assert qb.shape == (3, 128) and pad == 84 and shape == x.shape
     xr = quantization.dequantize_blockwise(qb, sb, zb, shape, pad)
     assert xr.shape == x.shape and (xr - x).abs().max() < 0.05
+
+
+def test_fast_round_half_away_identity():
+    """trunc(|v| + 0.49999997f) == floor(|v| + 0.5) for every float of interest (fp32 math).
+
+    The CUDA kernels round with this identity; check it on all .5 ties up to 2^23, their
+    float neighbours, and a dense sweep of [0, 4).
+    """
+    import numpy as np
+    c = np.float32(0.49999997)
+    assert c == np.nextafter(np.float32(0.5), np.float32(0))
+    k = np.arange(0, 1 << 23, dtype=np.float64)
+    ties = (k + 0.5).astype(np.float32)
+    ties = ties[(ties.astype(np.float64) == k + 0.5)]  # exactly representable ties
+    cand = np.concatenate([ties, np.nextafter(ties, np.float32(0)), np.nextafter(ties, np.float32(np.inf)),
+                           np.linspace(0, 4, 1 << 22, dtype=np.float32), np.float32([0.49999997, 0.5, 0.0])])
+    got = np.trunc(np.abs(cand) + c)  # fp32 add, fp32 trunc
+    want = np.floor(np.abs(cand).astype(np.float64) + 0.5)
+    assert got.dtype == np.float32
+    bad = np.nonzero(got.astype(np.float64) != want)[0]
+    assert bad.size == 0, cand[bad[:5]]

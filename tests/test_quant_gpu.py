@@ -62,3 +62,24 @@ def test_launches_on_current_stream(cuda_device):
         d = Q.dequantize(q, sc, z, 128, torch.float32)
     s.synchronize()
     assert (d - x).abs().max().item() < 0.1
+
+
+def test_rounding_ties_bit_exact(cuda_device):
+    """Codes of exact .5 ties and their neighbours (fp32 input, scale 1, zero point 0)."""
+    import numpy as np
+    vals = []
+    for k in range(0, 255):
+        t = np.float32(k + 0.5)
+        vals += [t, np.nextafter(t, np.float32(0)), np.nextafter(t, np.float32(1e9))]
+    vals += [np.float32(0.49999997)]
+    vals = [v for v in vals if 0 <= v <= 255]
+    groups = []
+    for i in range(0, len(vals), 126):
+        chunk = vals[i:i + 126]
+        chunk = chunk + [np.float32(1.0)] * (126 - len(chunk))
+        groups.append([np.float32(0.0), np.float32(255.0)] + chunk)
+    x = torch.tensor(np.array(groups, dtype=np.float32).reshape(-1), device=cuda_device)
+    q, s, z = Q.quantize(x, 8, 128, "asym", torch.float32)
+    q2, s2, z2 = spec.quantize_groups(x.cpu(), 8, 128, "asym", torch.float32)
+    assert bool((s2 == 1.0).all()) and bool((z2 == 0).all())
+    assert torch.equal(q.cpu(), q2)
