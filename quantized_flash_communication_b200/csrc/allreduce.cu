@@ -1,551 +1,21 @@
-// Fused quantized all-reduce over peer memory (NVLink 5 / NVSwitch): one kernel per call.
-//
-// Capability of the reference's flash_all_reduce (communication.py:7-97): the two-step
-// Flash-Communication all-reduce (quantize -> reduce-scatter -> dequant-sum -> requantize
-// -> all-gather -> dequantize) with INT8 / INT6 (INT4 + INT8) / INT4 / 16-bit payloads,
-// asymmetric or symmetric groups.  The reference runs it as ~7W+10 kernel launches, six
-// NCCL collectives and two host synchronisations per call; here it is a single launch:
-//
-//   phase 1  every CTA quantizes its 256-element units of every chunk in registers and
-//            stores the packed codes + per-group metadata straight into the chunk owner's
-//            reduce-scatter slot (plain st.global to the peer's mapped buffer), then
-//            publishes a per-(block, source) flag with a release store;
-//   phase 2  the owner CTA waits for the W flags of its block, dequant-sums the W
-//            contributions in fp32, requantizes, pushes the result into every peer's
-//            all-gather slot and writes its own chunk of the output;
-//   phase 3  after the all-gather flags, it dequantizes the other chunks into the output.
-//
-// CTA b of every rank handles the same unit indices, so each CTA only ever waits for
-// CTA b of the other ranks: no grid-wide barrier, and the grid is capped at the number
-// of co-resident CTAs so that every waited-for CTA is running.  Each wait is bounded by
-// %globaltimer; on expiry the CTA records the failure in a host-mapped status word and
-// returns.  A one-shot variant (every rank gathers every rank's quantized tensor and
-// sums locally, one round trip, one quantization) serves small, latency-bound messages.
-//
-// Epochs live in device memory (one counter per algorithm and block, advanced by the
-// kernel itself), so the launch is safe to capture in a CUDA graph and replay.
-//
-// Single-GPU emulation: with gridDim.y == W, block row y plays rank y, and every "peer"
-// buffer is a separate local allocation.  All W ranks then run inside one launch, which
-// lets the multi-rank protocol be exercised on one GPU.
-#include <ATen/ATen.h>
-#include <ATen/cuda/CUDAContext.h>
-#include <c10/cuda/CUDAGuard.h>
-#include <c10/cuda/CUDAException.h>
-
-#include <memory>
-
-#include "common.cuh"
-#include "workspace.h"
+// Host side of the fused quantized all-reduce: planning, argument checks, dispatch.
+// The kernels are in allreduce.cuh and are instantiated per input dtype in
+// allreduce_inst_*.cu (compiled in parallel).
+#include "allreduce.cuh"
 
 namespace qfc {
+namespace ar {
+#define QFC_AR_DECL(I, O)                                                                                  \
+  extern template void dispatch_bits<I, O>(const ARParams&, const Plan&, bool, int64_t, int, int, cudaStream_t);
+QFC_AR_DECL(__nv_bfloat16, __nv_bfloat16)
+QFC_AR_DECL(__nv_bfloat16, __half)
+QFC_AR_DECL(__half, __half)
+QFC_AR_DECL(float, float)
+QFC_AR_DECL(float, __half)
+#undef QFC_AR_DECL
+}  // namespace ar
 
-struct ARParams {
-  const void* in[kMaxRanks];
-  void* out[kMaxRanks];
-  char* base[kMaxRanks];
-  uint32_t* epochs[kMaxRanks];
-  KernelStatus* status;
-  int64_t n;       // elements
-  int64_t chunk;   // two-shot: elements per chunk; one-shot: n rounded up to 256
-  int64_t rs_off, ag_off, os_off, os_bytes;
-  int64_t slot1, slot2;  // slot strides in bytes (one-shot uses slot1)
-  int64_t pay1, pay2;    // payload bytes at the head of a slot; metadata follows
-  uint64_t timeout_ns;
-  int world, rank, gs, meta_fp32, sym, quantize_local;
-};
-
-namespace {
-
-QFC_DEV uint32_t* flag_at(char* base, int phase, int block, int src) {
-  return reinterpret_cast<uint32_t*>(base) + ((int64_t)(phase * kMaxBlocks + block) * kMaxRanks + src);
-}
-
-// One lane's 8 elements in wire form, plus its group's parameters.
-struct Enc8 {
-  uint4 a, b;
-  float s, z;
-};
-
-// Quantize 8 values given their group's (min, max).
-template <int P>
-QFC_DEV Enc8 encode_stats(const float (&v)[8], float mn, float mx, bool sym) {
-  Enc8 e;
-  e.a = make_uint4(0, 0, 0, 0);
-  e.b = make_uint4(0, 0, 0, 0);
-  float inv;
-  if (sym) QMath<P, true>::params(mn, mx, e.s, inv, e.z);
-  else QMath<P, false>::params(mn, mx, e.s, inv, e.z);
-  uint32_t m[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m[i] = QMath<P, false>::codebits(v[i], inv, e.z);
-  if constexpr (P == 8) {
-    const uint2 u = codebits8_to_u2(m);
-    e.a.x = u.x;
-    e.a.y = u.y;
-  } else {
-    e.a.x = codebits8_to_int4(m);
-  }
-  return e;
-}
-
-// Wire form of 8 fp32 values (group statistics from the values themselves).
-template <int P, typename WT>
-QFC_DEV Enc8 encode8(const float (&v)[8], int lpg, bool sym) {
-  if constexpr (P == 16) {
-    Enc8 e;
-    e.b = make_uint4(0, 0, 0, 0);
-    e.s = 1.f;
-    e.z = 0.f;
-    if constexpr (sizeof(WT) == 2) {
-      e.a = Vec8IO<WT>::pack(v);
-    } else {
-      e.a = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
-      e.b = make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]), __float_as_uint(v[7]));
-    }
-    return e;
-  } else {
-    float mn, mx;
-    group_minmax_f32(v, lpg, mn, mx);
-    return encode_stats<P>(v, mn, mx, sym);
-  }
-}
-
-// Wire form of 8 raw input elements; 16-bit inputs reduce their group statistics on the
-// packed values.  v receives the fp32 values.
-template <int P, typename WT>
-QFC_DEV Enc8 encode_raw(const Raw8<WT>& r, int lpg, bool sym, float (&v)[8]) {
-  raw8_to_f32(r, v);
-  if constexpr (P == 16) {
-    Enc8 e;
-    e.a = r.a;
-    e.b = r.b;
-    e.s = 1.f;
-    e.z = 0.f;
-    return e;
-  } else if constexpr (sizeof(WT) == 2) {
-    float mn, mx;
-    group_minmax16<WT>(r.a, lpg, mn, mx);
-    return encode_stats<P>(v, mn, mx, sym);
-  } else {
-    return encode8<P, WT>(v, lpg, sym);
-  }
-}
-
-template <int P, typename WT>
-QFC_DEV void store8(char* slot, char* meta, int64_t loc, const Enc8& e, bool leader, int gs, int meta_fp32) {
-  if constexpr (P == 16) {
-    if constexpr (sizeof(WT) == 2) {
-      *reinterpret_cast<uint4*>(slot + loc * 2) = e.a;
-    } else {
-      uint4* d = reinterpret_cast<uint4*>(slot + loc * 4);
-      d[0] = e.a;
-      d[1] = e.b;
-    }
-  } else {
-    if constexpr (P == 8) *reinterpret_cast<uint2*>(slot + loc) = make_uint2(e.a.x, e.a.y);
-    else *reinterpret_cast<uint32_t*>(slot + (loc >> 1)) = e.a.x;
-    if (leader) {
-      const int64_t g = loc / gs;
-      if (meta_fp32) *reinterpret_cast<float2*>(meta + g * 8) = make_float2(e.s, e.z);
-      else *reinterpret_cast<uint32_t*>(meta + g * 4) = pack_f16x2(e.s, e.z);
-    }
-  }
-}
-
-// Values a receiver reconstructs from an Enc8 (uses the scale as stored on the wire).
-template <int P, typename WT>
-QFC_DEV void decode8(const Enc8& e, int meta_fp32, float (&d)[8]) {
-  if constexpr (P == 16) {
-    if constexpr (sizeof(WT) == 2) {
-      const uint32_t w[4] = {e.a.x, e.a.y, e.a.z, e.a.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if constexpr (std::is_same<WT, __nv_bfloat16>::value) unpack_bf16x2(w[i], d[2 * i], d[2 * i + 1]);
-        else unpack_f16x2(w[i], d[2 * i], d[2 * i + 1]);
-      }
-    } else {
-      d[0] = __uint_as_float(e.a.x); d[1] = __uint_as_float(e.a.y);
-      d[2] = __uint_as_float(e.a.z); d[3] = __uint_as_float(e.a.w);
-      d[4] = __uint_as_float(e.b.x); d[5] = __uint_as_float(e.b.y);
-      d[6] = __uint_as_float(e.b.z); d[7] = __uint_as_float(e.b.w);
-    }
-  } else {
-    const float ss = meta_fp32 ? e.s : __half2float(__float2half_rn(e.s));
-    if constexpr (P == 8) dq_u2(make_uint2(e.a.x, e.a.y), e.z, ss, d);
-    else dq_u2(int4_to_u2(e.a.x), e.z, ss, d);
-  }
-}
-
-// One lane's 8 elements as they sit in a slot: payload words + the group's metadata.
-struct Wire8 {
-  uint4 a, b;
-  float s, z;
-};
-
-// Read a lane's wire data from a slot in local memory (L2, bypassing L1: the bytes were
-// written by another GPU).  Separate from decoding so that a warp can put the loads of
-// all W slots in flight before it uses any of them.
-template <int P, typename WT>
-QFC_DEV Wire8 load_wire(const char* slot, const char* meta, int64_t loc, int gs, int meta_fp32) {
-  Wire8 w;
-  w.b = make_uint4(0, 0, 0, 0);
-  w.s = 1.f;
-  w.z = 0.f;
-  if constexpr (P == 16) {
-    const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const WT*>(slot) + loc);
-    w.a = __ldcg(p);
-    if constexpr (sizeof(WT) == 4) w.b = __ldcg(p + 1);
-  } else {
-    const int64_t g = loc / gs;
-    if (meta_fp32) {
-      const float2 m = __ldcg(reinterpret_cast<const float2*>(meta + g * 8));
-      w.s = m.x;
-      w.z = m.y;
-    } else {
-      const uint32_t m = __ldcg(reinterpret_cast<const unsigned int*>(meta + g * 4));
-      w.s = __uint_as_float(m);  // unpacked in decode_wire
-    }
-    if constexpr (P == 8) {
-      const uint2 u = __ldcg(reinterpret_cast<const uint2*>(slot + loc));
-      w.a = make_uint4(u.x, u.y, 0, 0);
-    } else {
-      w.a = make_uint4(__ldcg(reinterpret_cast<const unsigned int*>(slot + (loc >> 1))), 0, 0, 0);
-    }
-  }
-  return w;
-}
-
-template <int P, typename WT>
-QFC_DEV void decode_wire(const Wire8& w, int meta_fp32, float (&d)[8]) {
-  if constexpr (P == 16) {
-    Raw8<WT> r;
-    r.a = w.a;
-    r.b = w.b;
-    raw8_to_f32<WT>(r, d);
-  } else {
-    float s = w.s, z = w.z;
-    if (!meta_fp32) unpack_f16x2(__float_as_uint(w.s), s, z);
-    if constexpr (P == 8) dq_u2(make_uint2(w.a.x, w.a.y), z, s, d);
-    else dq_u2(int4_to_u2(w.a.x), z, s, d);
-  }
-}
-
-// Threads 0..W-1 each wait for one source's flag; returns false (for the whole CTA)
-// if any wait ran out.  skip_self: the own flag is not waited for.
-QFC_DEV bool wait_sources(const ARParams& p, char* my, int phase, int b, int rank, int W, uint32_t e,
-                          bool skip_self, int* s_abort) {
-  if ((int)threadIdx.x < W && !(skip_self && (int)threadIdx.x == rank)) {
-    uint32_t seen = 0;
-    const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
-    if (!wait_flag_geq(flag_at(my, phase, b, threadIdx.x), e, deadline, seen)) {
-      report_timeout(p.status, phase, b, threadIdx.x, e, seen);
-      *s_abort = 1;
-    }
-  }
-  __syncthreads();
-  return *s_abort == 0;
-}
-
-template <typename InT, typename OutT, int P1, int P2>
-__global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ ARParams p) {
-  const int rank = gridDim.y > 1 ? (int)blockIdx.y : p.rank;
-  const int W = p.world;
-  const int b = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
-  const int lpg = p.gs >> 3;
-  const bool leader = (lane & (lpg - 1)) == 0;
-  const InT* in = static_cast<const InT*>(p.in[rank]);
-  OutT* out = static_cast<OutT*>(p.out[rank]);
-  char* my = p.base[rank];
-  uint32_t* ep = p.epochs[rank] + ALG_TWO_SHOT * kMaxBlocks + b;
-  __shared__ uint32_t s_e;
-  __shared__ int s_abort;
-  if (threadIdx.x == 0) {
-    s_e = *ep + 1u;
-    s_abort = 0;
-  }
-  __syncthreads();
-  const uint32_t e = s_e;
-  const int64_t C = p.chunk;
-  const int64_t units = C >> 8;
-  const int64_t ustride = (int64_t)gridDim.x * wpb;
-  const int64_t u0 = (int64_t)b * wpb + warp;
-
-  // Phase 1: quantize every chunk's units of this block, push to the chunk's owner.
-  // All W chunk loads of a unit are issued before any of them is used.
-  for (int64_t u = u0; u < units; u += ustride) {
-    const int64_t loc = (u << 8) + lane * 8;
-    Raw8<InT> raw[kMaxRanks];
-#pragma unroll
-    for (int jj = 0; jj < kMaxRanks; ++jj) {
-      if (jj < W) {
-        const int j = (rank + 1 + jj) % W;  // peers staggered, own chunk last
-        raw[jj] = load_raw8(in, (int64_t)j * C + loc, p.n);
-      }
-    }
-#pragma unroll
-    for (int jj = 0; jj < kMaxRanks; ++jj) {
-      if (jj < W) {
-        const int j = (rank + 1 + jj) % W;
-        if (j == rank && !p.quantize_local) continue;
-        float v[8];
-        const Enc8 en = encode_raw<P1, InT>(raw[jj], lpg, p.sym, v);
-        char* slot = p.base[j] + p.rs_off + (int64_t)rank * p.slot1;
-        store8<P1, InT>(slot, slot + p.pay1, loc, en, leader, p.gs, p.meta_fp32);
-      }
-    }
-  }
-  __syncthreads();
-  if ((int)threadIdx.x < W) st_release_sys(flag_at(p.base[threadIdx.x], PH_RS, b, rank), e);
-  if (!wait_sources(p, my, PH_RS, b, rank, W, e, false, &s_abort)) return;
-
-  // Phase 2: reduce the own chunk, requantize, push to every peer, write own output.
-  for (int64_t u = u0; u < units; u += ustride) {
-    const int64_t loc = (u << 8) + lane * 8;
-    Wire8 wv[kMaxRanks];
-#pragma unroll
-    for (int s = 0; s < kMaxRanks; ++s) {
-      if (s < W && !(s == rank && !p.quantize_local)) {
-        const char* slot = my + p.rs_off + (int64_t)s * p.slot1;
-        wv[s] = load_wire<P1, InT>(slot, slot + p.pay1, loc, p.gs, p.meta_fp32);
-      }
-    }
-    float acc[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-#pragma unroll
-    for (int s = 0; s < kMaxRanks; ++s) {
-      if (s < W) {
-        float d[8];
-        if (s == rank && !p.quantize_local) load8_guard(in, (int64_t)rank * C + loc, p.n, d);
-        else decode_wire<P1, InT>(wv[s], p.meta_fp32, d);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], d[i]);
-      }
-    }
-    const Enc8 en = encode8<P2, InT>(acc, lpg, p.sym);
-#pragma unroll
-    for (int jj = 1; jj < kMaxRanks; ++jj) {
-      if (jj < W) {
-        const int j = (rank + jj) % W;
-        char* slot = p.base[j] + p.ag_off + (int64_t)rank * p.slot2;
-        store8<P2, InT>(slot, slot + p.pay2, loc, en, leader, p.gs, p.meta_fp32);
-      }
-    }
-    float o[8];
-    decode8<P2, InT>(en, p.meta_fp32, o);
-    store8_guard(out, (int64_t)rank * C + loc, p.n, o);
-  }
-  __syncthreads();
-  if ((int)threadIdx.x < W && (int)threadIdx.x != rank)
-    st_release_sys(flag_at(p.base[threadIdx.x], PH_AG, b, rank), e);
-  if (!wait_sources(p, my, PH_AG, b, rank, W, e, true, &s_abort)) return;
-
-  // Phase 3: dequantize the gathered chunks of the other ranks.
-  for (int64_t u = u0; u < units; u += ustride) {
-    const int64_t loc = (u << 8) + lane * 8;
-    Wire8 wv[kMaxRanks];
-#pragma unroll
-    for (int jj = 1; jj < kMaxRanks; ++jj) {
-      if (jj < W) {
-        const int j = (rank + jj) % W;
-        const char* slot = my + p.ag_off + (int64_t)j * p.slot2;
-        wv[jj] = load_wire<P2, InT>(slot, slot + p.pay2, loc, p.gs, p.meta_fp32);
-      }
-    }
-#pragma unroll
-    for (int jj = 1; jj < kMaxRanks; ++jj) {
-      if (jj < W) {
-        const int j = (rank + jj) % W;
-        float d[8];
-        decode_wire<P2, InT>(wv[jj], p.meta_fp32, d);
-        store8_guard(out, (int64_t)j * C + loc, p.n, d);
-      }
-    }
-  }
-  if (threadIdx.x == 0) *ep = e;
-}
-
-template <typename InT, typename OutT, int P>
-__global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ ARParams p) {
-  const int rank = gridDim.y > 1 ? (int)blockIdx.y : p.rank;
-  const int W = p.world;
-  const int b = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
-  const int lpg = p.gs >> 3;
-  const bool leader = (lane & (lpg - 1)) == 0;
-  const InT* in = static_cast<const InT*>(p.in[rank]);
-  OutT* out = static_cast<OutT*>(p.out[rank]);
-  char* my = p.base[rank];
-  uint32_t* ep = p.epochs[rank] + ALG_ONE_SHOT * kMaxBlocks + b;
-  __shared__ uint32_t s_e;
-  __shared__ int s_abort;
-  if (threadIdx.x == 0) {
-    s_e = *ep + 1u;
-    s_abort = 0;
-  }
-  __syncthreads();
-  const uint32_t e = s_e;
-  // Double-buffered by epoch parity: a peer may start call k+1 while this rank still
-  // reads call k's slots.
-  const int64_t region = p.os_off + (int64_t)(e & 1u) * p.os_bytes;
-  const int64_t units = p.chunk >> 8;
-  const int64_t ustride = (int64_t)gridDim.x * wpb;
-  const int64_t u0 = (int64_t)b * wpb + warp;
-
-  for (int64_t u = u0; u < units; u += ustride) {
-    const int64_t loc = (u << 8) + lane * 8;
-    float v[8];
-    const Enc8 en = encode_raw<P, InT>(load_raw8(in, loc, p.n), lpg, p.sym, v);
-#pragma unroll
-    for (int jj = 1; jj < kMaxRanks; ++jj) {
-      if (jj < W) {
-        const int j = (rank + jj) % W;
-        char* slot = p.base[j] + region + (int64_t)rank * p.slot1;
-        store8<P, InT>(slot, slot + p.pay1, loc, en, leader, p.gs, p.meta_fp32);
-      }
-    }
-  }
-  __syncthreads();
-  if ((int)threadIdx.x < W && (int)threadIdx.x != rank)
-    st_release_sys(flag_at(p.base[threadIdx.x], PH_OS, b, rank), e);
-  if (!wait_sources(p, my, PH_OS, b, rank, W, e, true, &s_abort)) return;
-
-  for (int64_t u = u0; u < units; u += ustride) {
-    const int64_t loc = (u << 8) + lane * 8;
-    Wire8 wv[kMaxRanks];
-#pragma unroll
-    for (int s = 0; s < kMaxRanks; ++s) {
-      if (s < W && s != rank) {
-        const char* slot = my + region + (int64_t)s * p.slot1;
-        wv[s] = load_wire<P, InT>(slot, slot + p.pay1, loc, p.gs, p.meta_fp32);
-      }
-    }
-    float own[8];
-    const Enc8 en_own = encode_raw<P, InT>(load_raw8(in, loc, p.n), lpg, p.sym, own);
-    if (p.quantize_local) decode8<P, InT>(en_own, p.meta_fp32, own);
-    float acc[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-#pragma unroll
-    for (int s = 0; s < kMaxRanks; ++s) {
-      if (s < W) {
-        float d[8];
-        if (s == rank) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) d[i] = own[i];
-        } else {
-          decode_wire<P, InT>(wv[s], p.meta_fp32, d);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], d[i]);
-      }
-    }
-    store8_guard(out, loc, p.n, acc);
-  }
-  if (threadIdx.x == 0) *ep = e;
-}
-
-// ---------------------------------------------------------------------------------------
-// Host side
-// ---------------------------------------------------------------------------------------
-struct Plan {
-  int p1, p2;
-  int64_t chunk, slot1, slot2, pay1, pay2;
-  int64_t need_rs, need_ag, need_os;
-};
-
-int64_t payload_bytes(int64_t elems, int P, int in_elem) {
-  if (P == 16) return elems * in_elem;
-  return P == 8 ? elems : elems / 2;
-}
-int64_t meta_bytes(int64_t elems, int P, int gs, bool fp32) {
-  if (P == 16) return 0;
-  return (elems / gs) * (fp32 ? 8 : 4);
-}
-
-void phase_bits(int bits, int& p1, int& p2) {
-  switch (bits) {
-    case 16: p1 = 16; p2 = 16; break;
-    case 8: p1 = 8; p2 = 8; break;
-    case 6: p1 = 4; p2 = 8; break;
-    case 4: p1 = 4; p2 = 4; break;
-    default: TORCH_CHECK(false, "quant_all_reduce: bits must be 16, 8, 6 or 4; got ", bits);
-  }
-}
-
-Plan make_plan(int64_t n, int W, int bits, int gs, bool fp32, int in_elem, bool one_shot) {
-  Plan pl;
-  phase_bits(bits, pl.p1, pl.p2);
-  if (one_shot) {
-    // A single quantization step; INT6 uses its wider (INT8) half.
-    const int P = (bits == 6) ? 8 : pl.p1;
-    pl.p1 = pl.p2 = P;
-    pl.chunk = align_up(std::max<int64_t>(n, 1), 256);
-    pl.pay1 = align_up(payload_bytes(pl.chunk, P, in_elem), 256);
-    pl.slot1 = pl.pay1 + align_up(meta_bytes(pl.chunk, P, gs, fp32), 256);
-    pl.pay2 = pl.pay1;
-    pl.slot2 = pl.slot1;
-    pl.need_rs = pl.need_ag = 0;
-    pl.need_os = (int64_t)W * pl.slot1;
-  } else {
-    pl.chunk = align_up((std::max<int64_t>(n, 1) + W - 1) / W, 256);
-    pl.pay1 = align_up(payload_bytes(pl.chunk, pl.p1, in_elem), 256);
-    pl.slot1 = pl.pay1 + align_up(meta_bytes(pl.chunk, pl.p1, gs, fp32), 256);
-    pl.pay2 = align_up(payload_bytes(pl.chunk, pl.p2, in_elem), 256);
-    pl.slot2 = pl.pay2 + align_up(meta_bytes(pl.chunk, pl.p2, gs, fp32), 256);
-    pl.need_rs = (int64_t)W * pl.slot1;
-    pl.need_ag = (int64_t)W * pl.slot2;
-    pl.need_os = 0;
-  }
-  return pl;
-}
-
-int num_sms(int dev) {
-  static int cached[64] = {0};
-  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
-  int v = 0;
-  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-  if (dev >= 0 && dev < 64) cached[dev] = v;
-  return v;
-}
-
-template <typename Kern>
-void launch_ar(Kern kern, const ARParams& prm, int64_t units, int W_emul, int dev, cudaStream_t st) {
-  const int sms = num_sms(dev);
-  int wpb = (int)std::min<int64_t>(16, std::max<int64_t>(2, (units + sms - 1) / sms));
-  const int threads = wpb * 32;
-  int occ = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, 0);
-  if (occ < 1) occ = 1;
-  int64_t cap = (int64_t)occ * sms / std::max(1, W_emul);
-  cap = std::min<int64_t>(cap, std::min<int64_t>(sms, kMaxBlocks));
-  TORCH_CHECK(cap >= 1, "quant_all_reduce: no co-resident CTA budget (emulated world too large)");
-  const int64_t G = std::max<int64_t>(1, std::min<int64_t>((units + wpb - 1) / wpb, cap));
-  dim3 grid((unsigned)G, (unsigned)std::max(1, W_emul));
-  kern<<<grid, threads, 0, st>>>(prm);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-template <typename InT, typename OutT>
-void dispatch_bits(const ARParams& prm, const Plan& pl, bool one_shot, int64_t units, int W_emul, int dev,
-                   cudaStream_t st) {
-  if (one_shot) {
-    switch (pl.p1) {
-      case 16: launch_ar(one_shot_kernel<InT, OutT, 16>, prm, units, W_emul, dev, st); break;
-      case 8: launch_ar(one_shot_kernel<InT, OutT, 8>, prm, units, W_emul, dev, st); break;
-      default: launch_ar(one_shot_kernel<InT, OutT, 4>, prm, units, W_emul, dev, st); break;
-    }
-    return;
-  }
-  if (pl.p1 == 16) launch_ar(two_shot_kernel<InT, OutT, 16, 16>, prm, units, W_emul, dev, st);
-  else if (pl.p1 == 8) launch_ar(two_shot_kernel<InT, OutT, 8, 8>, prm, units, W_emul, dev, st);
-  else if (pl.p2 == 8) launch_ar(two_shot_kernel<InT, OutT, 4, 8>, prm, units, W_emul, dev, st);
-  else launch_ar(two_shot_kernel<InT, OutT, 4, 4>, prm, units, W_emul, dev, st);
-}
-
-}  // namespace
+using namespace ar;
 
 using WsPtr = std::shared_ptr<Workspace>;
 

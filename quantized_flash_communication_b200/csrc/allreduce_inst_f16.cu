@@ -1,0 +1,8 @@
+// Explicit instantiations of the fused all-reduce kernels for f16 inputs.
+#include "allreduce.cuh"
+
+namespace qfc {
+namespace ar {
+template void dispatch_bits<__half, __half>(const ARParams&, const Plan&, bool, int64_t, int, int, cudaStream_t);
+}  // namespace ar
+}  // namespace qfc

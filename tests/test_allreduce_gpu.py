@@ -35,6 +35,9 @@ CASES = [
     (4, 4, 64, "asym", (1, 4096), "two_shot"),
     (8, 16, 128, "asym", (1024, 4096), "two_shot"),
     (1, 8, 128, "asym", (5, 4096), "two_shot"),
+    (3, 8, 128, "asym", (37, 4096), "two_shot"),   # generic (runtime world size) kernels
+    (5, 6, 64, "sym", (9, 1000), "two_shot"),
+    (3, 4, 128, "asym", (5, 4096), "one_shot"),
     (2, 8, 128, "asym", (1, 4096), "one_shot"),
     (8, 8, 128, "asym", (64, 4096), "one_shot"),
     (8, 4, 128, "sym", (7, 999), "one_shot"),
