@@ -92,6 +92,7 @@ void quant_all_reduce(const std::vector<WsPtr>& wss, const std::vector<at::Tenso
   prm.world = W;
   prm.rank = emulate ? 0 : (int)w0.rank();
   prm.gs = (int)gs;
+  prm.gs_shift = __builtin_ctz((unsigned)gs);
   prm.meta_fp32 = scale_fp32 ? 1 : 0;
   prm.sym = sym ? 1 : 0;
   prm.quantize_local = quantize_local ? 1 : 0;

@@ -53,7 +53,7 @@ struct ARParams {
   int64_t slot1, slot2;  // slot strides in bytes (one-shot uses slot1)
   int64_t pay1, pay2;    // payload bytes at the head of a slot; metadata follows
   uint64_t timeout_ns;
-  int world, rank, gs, meta_fp32, sym, quantize_local;
+  int world, rank, gs, gs_shift, meta_fp32, sym, quantize_local;
 };
 
 namespace ar {
@@ -134,7 +134,7 @@ QFC_DEV Enc8 encode_raw(const Raw8<WT>& r, int lpg, bool sym, float (&v)[8]) {
 }
 
 template <int P, typename WT>
-QFC_DEV void store8(char* slot, char* meta, int64_t loc, const Enc8& e, bool leader, int gs, int meta_fp32) {
+QFC_DEV void store8(char* slot, char* meta, int64_t loc, const Enc8& e, bool leader, int gs_shift, int meta_fp32) {
   if constexpr (P == 16) {
     if constexpr (sizeof(WT) == 2) {
       *reinterpret_cast<uint4*>(slot + loc * 2) = e.a;
@@ -147,7 +147,7 @@ QFC_DEV void store8(char* slot, char* meta, int64_t loc, const Enc8& e, bool lea
     if constexpr (P == 8) *reinterpret_cast<uint2*>(slot + loc) = make_uint2(e.a.x, e.a.y);
     else *reinterpret_cast<uint32_t*>(slot + (loc >> 1)) = e.a.x;
     if (leader) {
-      const int64_t g = loc / gs;
+      const int64_t g = loc >> gs_shift;
       if (meta_fp32) *reinterpret_cast<float2*>(meta + g * 8) = make_float2(e.s, e.z);
       else *reinterpret_cast<uint32_t*>(meta + g * 4) = pack_f16x2(e.s, e.z);
     }
@@ -188,7 +188,7 @@ struct Wire8 {
 // written by another GPU).  Separate from decoding so that a warp can put the loads of
 // all W slots in flight before it uses any of them.
 template <int P, typename WT>
-QFC_DEV Wire8 load_wire(const char* slot, const char* meta, int64_t loc, int gs, int meta_fp32) {
+QFC_DEV Wire8 load_wire(const char* slot, const char* meta, int64_t loc, int gs_shift, int meta_fp32) {
   Wire8 w;
   w.b = make_uint4(0, 0, 0, 0);
   w.s = 1.f;
@@ -198,7 +198,7 @@ QFC_DEV Wire8 load_wire(const char* slot, const char* meta, int64_t loc, int gs,
     w.a = __ldcg(p);
     if constexpr (sizeof(WT) == 4) w.b = __ldcg(p + 1);
   } else {
-    const int64_t g = loc / gs;
+    const int64_t g = loc >> gs_shift;
     if (meta_fp32) {
       const float2 m = __ldcg(reinterpret_cast<const float2*>(meta + g * 8));
       w.s = m.x;
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ A
           float v[8];
           const Enc8 en = encode_raw<P1, InT>(raw[k], lpg, p.sym, v);
           char* slot = p.base[j] + p.rs_off + (int64_t)rank * p.slot1;
-          store8<P1, InT>(slot, slot + p.pay1, loc, en, leader, p.gs, p.meta_fp32);
+          store8<P1, InT>(slot, slot + p.pay1, loc, en, leader, p.gs_shift, p.meta_fp32);
         }
       }
     }
@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ A
           for (int s = 0; s < NW; ++s) {
             if (s < W && !(s == rank && !p.quantize_local)) {
               const char* slot = my + p.rs_off + (int64_t)s * p.slot1;
-              wv[a][s] = load_wire<P1, InT>(slot, slot + p.pay1, loc, p.gs, p.meta_fp32);
+              wv[a][s] = load_wire<P1, InT>(slot, slot + p.pay1, loc, p.gs_shift, p.meta_fp32);
             }
           }
         }
@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ A
             if (jj < W) {
               const int j = (rank + jj) % W;
               char* slot = p.base[j] + p.ag_off + (int64_t)rank * p.slot2;
-              store8<P2, InT>(slot, slot + p.pay2, loc, en, leader, p.gs, p.meta_fp32);
+              store8<P2, InT>(slot, slot + p.pay2, loc, en, leader, p.gs_shift, p.meta_fp32);
             }
           }
           float o[8];
@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ A
           const int j = (rank + 1 + jj) % W;
           const int64_t loc = ((u0 + i * ustride) << 8) + lane_off;
           const char* slot = my + p.ag_off + (int64_t)j * p.slot2;
-          wv[k] = load_wire<P2, InT>(slot, slot + p.pay2, loc, p.gs, p.meta_fp32);
+          wv[k] = load_wire<P2, InT>(slot, slot + p.pay2, loc, p.gs_shift, p.meta_fp32);
         }
       }
 #pragma unroll
@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ A
           if (jj < W) {
             const int j = (rank + jj) % W;
             char* slot = p.base[j] + region + (int64_t)rank * p.slot1;
-            store8<P, InT>(slot, slot + p.pay1, loc, en, leader, p.gs, p.meta_fp32);
+            store8<P, InT>(slot, slot + p.pay1, loc, en, leader, p.gs_shift, p.meta_fp32);
           }
         }
       }
@@ -493,7 +493,7 @@ __global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ A
         for (int s = 0; s < NW; ++s) {
           if (s < W && s != rank) {
             const char* slot = my + region + (int64_t)s * p.slot1;
-            wv[a][s] = load_wire<P, InT>(slot, slot + p.pay1, loc, p.gs, p.meta_fp32);
+            wv[a][s] = load_wire<P, InT>(slot, slot + p.pay1, loc, p.gs_shift, p.meta_fp32);
           }
         }
       }

@@ -44,9 +44,18 @@ quantize_kernel(const T* __restrict__ x, uint8_t* __restrict__ q, ST* __restrict
   if (gs <= 256) {
     const int lpg = gs >> 3;  // lanes per group
     const int64_t n_units = (n + 255) / 256;
-    for (int64_t u = warp; u < n_units; u += nwarps) {
+    constexpr int kUnroll = 4;  // independent loads in flight per lane
+    for (int64_t ub = warp; ub < n_units; ub += kUnroll * nwarps) {
+     Raw8<T> raws[kUnroll];
+#pragma unroll
+     for (int k = 0; k < kUnroll; ++k)
+       if (ub + k * nwarps < n_units) raws[k] = load_raw8(x, (ub + k * nwarps) * 256 + lane * 8, n);
+#pragma unroll
+     for (int k = 0; k < kUnroll; ++k) {
+      const int64_t u = ub + k * nwarps;
+      if (u >= n_units) break;
       const int64_t idx = u * 256 + lane * 8;
-      const Raw8<T> raw = load_raw8(x, idx, n);
+      const Raw8<T>& raw = raws[k];
       float v[8];
       raw8_to_f32(raw, v);
       float mn, mx;
@@ -65,10 +74,11 @@ quantize_kernel(const T* __restrict__ x, uint8_t* __restrict__ q, ST* __restrict
           if (idx + i < n) q[idx + i] = (uint8_t)(m[i] & 0xffu);
       }
       if ((lane & (lpg - 1)) == 0 && idx < n) {
-        const int64_t g = idx / gs;
+        const int64_t g = idx >> (__ffs(gs) - 1);
         store_scale<ST>(s_out + g, s);
         z_out[g] = __float2half_rn(z);
       }
+     }
     }
   } else {
     const int64_t n_groups = (n + gs - 1) / gs;
@@ -142,9 +152,10 @@ template <typename QT, typename ST, typename OT>
 __global__ void __launch_bounds__(kThreads)
 dequantize_kernel(const QT* __restrict__ q, const ST* __restrict__ s, const __half* __restrict__ z,
                   OT* __restrict__ out, int64_t n, int gs) {
+  const int gsh = __ffs(gs) - 1;  // group sizes are powers of two
   const int64_t stride = (int64_t)gridDim.x * blockDim.x * 8;
   for (int64_t idx = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; idx < n; idx += stride) {
-    const int64_t g = idx / gs;
+    const int64_t g = idx >> gsh;
     const float sc = to_f32(s[g]);
     const float zz = __half2float(z[g]);
     float v[8];
