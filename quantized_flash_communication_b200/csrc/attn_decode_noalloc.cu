@@ -1,0 +1,128 @@
+// Allocation-free entry point of the paged decode attention (declared in qfc_noalloc.h).
+//
+// No counterpart in the reference.  It runs the same two kernels as attn_decode.cu (split-KV
+// partials, then their merge) but takes the fp32 partials from a fixed array compiled
+// into the library, so a caller that may not allocate device memory (a runtime with its
+// own memory pool, a plugin inside one, C code without PyTorch's allocator) can use it.
+// The array's size limits batch x heads x context; larger calls are refused.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "attn_decode_kernels.cuh"
+#include "qfc_noalloc.h"
+
+namespace {
+
+using namespace qfc::decode;
+
+// The scratch shared by every call on a device: fp32 partial outputs then (max, sum) pairs.
+static __device__ __align__(256) float qfc_noalloc_scratch[QFC_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+float* g_scratch[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device, looked up once per device.
+// In host code the array's name is only a host-side stand-in; passing it to a kernel
+// would be wrong, so the address always comes from cudaGetSymbolAddress.
+int scratch_for_current_device(float** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QFC_NOALLOC_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_scratch[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, qfc_noalloc_scratch) != cudaSuccess || p == nullptr) return QFC_NOALLOC_ERR_CUDA;
+    g_scratch[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch[dev];
+  return QFC_NOALLOC_OK;
+}
+
+unsigned long long needed_bytes(int batch, int nq, int hd, int page, int max_pages) {
+  const unsigned long long parts = ((unsigned long long)max_pages * page + kPart - 1) / kPart;
+  return (unsigned long long)batch * nq * parts * (hd + 2) * sizeof(float);
+}
+
+template <typename T, int HD, int G>
+int launch(const void* q, const void* kc, const void* vc, const int* bt, const int* sl, void* out, int B, int nq,
+           int nkv, int page, int max_pages, float scale, float* scratch, cudaStream_t st) {
+  const int n_parts = (max_pages * page + kPart - 1) / kPart;
+  float* part_o = scratch;
+  float* part_ml = scratch + (size_t)B * nq * n_parts * HD;
+  dim3 grid(n_parts, nkv, B);
+  decode_partial_kernel<T, HD, G><<<grid, kWarps * 32, 0, st>>>(
+      static_cast<const T*>(q), static_cast<const T*>(kc), static_cast<const T*>(vc), bt, sl, part_o, part_ml, nq, nkv,
+      page, max_pages, n_parts, scale);
+  const int warps = B * nq;
+  decode_combine_kernel<T, HD><<<(warps * 32 + 255) / 256, 256, 0, st>>>(part_o, part_ml, sl, static_cast<T*>(out),
+                                                                           nq, n_parts, warps);
+  return cudaGetLastError() == cudaSuccess ? QFC_NOALLOC_OK : QFC_NOALLOC_ERR_CUDA;
+}
+
+template <typename T>
+int dispatch(int hd, int G, const void* q, const void* kc, const void* vc, const int* bt, const int* sl, void* out,
+             int B, int nq, int nkv, int page, int max_pages, float scale, float* scratch, cudaStream_t st) {
+#define QFC_NA(HD_, G_) return launch<T, HD_, G_>(q, kc, vc, bt, sl, out, B, nq, nkv, page, max_pages, scale, scratch, st)
+  if (hd == 128) {
+    switch (G) {
+      case 1: QFC_NA(128, 1);
+      case 2: QFC_NA(128, 2);
+      case 4: QFC_NA(128, 4);
+      case 8: QFC_NA(128, 8);
+    }
+  } else if (hd == 64) {
+    switch (G) {
+      case 1: QFC_NA(64, 1);
+      case 2: QFC_NA(64, 2);
+      case 4: QFC_NA(64, 4);
+      case 8: QFC_NA(64, 8);
+    }
+  }
+#undef QFC_NA
+  return QFC_NOALLOC_ERR_BAD_ARGS;
+}
+
+}  // namespace
+
+extern "C" {
+
+unsigned long long qfc_attn_decode_noalloc_scratch_bytes(int batch, int num_q_heads, int head_dim, int page_size,
+                                                         int max_pages_per_seq) {
+  return needed_bytes(batch, num_q_heads, head_dim, page_size, max_pages_per_seq);
+}
+
+int qfc_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const int* block_table,
+                            const int* seq_lens, void* out, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                            int page_size, int max_pages_per_seq, float scale, int dtype, cudaStream_t stream) {
+  if (!q || !k_cache || !v_cache || !block_table || !seq_lens || !out) return QFC_NOALLOC_ERR_BAD_ARGS;
+  if (batch <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0 || page_size <= 0 || max_pages_per_seq <= 0)
+    return QFC_NOALLOC_ERR_BAD_ARGS;
+  if (needed_bytes(batch, num_q_heads, head_dim, page_size, max_pages_per_seq) > QFC_NOALLOC_SCRATCH_BYTES)
+    return QFC_NOALLOC_ERR_TOO_LARGE;
+  float* scratch = nullptr;
+  const int rc = scratch_for_current_device(&scratch);
+  if (rc != QFC_NOALLOC_OK) return rc;
+  const int G = num_q_heads / num_kv_heads;
+  if (dtype == 0)
+    return dispatch<__nv_bfloat16>(head_dim, G, q, k_cache, v_cache, block_table, seq_lens, out, batch, num_q_heads,
+                                   num_kv_heads, page_size, max_pages_per_seq, scale, scratch, stream);
+  if (dtype == 1)
+    return dispatch<__half>(head_dim, G, q, k_cache, v_cache, block_table, seq_lens, out, batch, num_q_heads,
+                            num_kv_heads, page_size, max_pages_per_seq, scale, scratch, stream);
+  return QFC_NOALLOC_ERR_BAD_ARGS;
+}
+
+const char* qfc_noalloc_error_string(int code) {
+  switch (code) {
+    case QFC_NOALLOC_OK: return "ok";
+    case QFC_NOALLOC_ERR_TOO_LARGE:
+      return "call needs more scratch than the 16 MiB compiled into the library "
+             "(batch * q_heads * ceil(max_pages * page / 256) * (head_dim + 2) * 4 bytes)";
+    case QFC_NOALLOC_ERR_BAD_ARGS: return "bad arguments (null pointer, head_dim not 64/128, GQA group not 1/2/4/8, dtype)";
+    case QFC_NOALLOC_ERR_CUDA: return "a CUDA runtime call failed";
+    default: return "unknown error code";
+  }
+}
+
+}  // extern "C"
