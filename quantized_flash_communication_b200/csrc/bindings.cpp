@@ -43,6 +43,10 @@ void argmax_cuda(const at::Tensor& logits, at::Tensor& best_val, at::Tensor& bes
 // attn_decode.cu
 void attn_decode_cuda(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& bt,
                       const at::Tensor& sl, at::Tensor& out, int64_t nq, int64_t nkv, int64_t hd, double scale);
+// attn_prefill.cu
+void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_t S, int64_t nq, int64_t nkv,
+                       int64_t hd, double scale);
+int64_t attn_status(bool clear);
 }  // namespace qfc
 
 namespace py = pybind11;
@@ -90,6 +94,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &qfc::embedding_cuda);
   m.def("argmax", &qfc::argmax_cuda);
   m.def("attn_decode", &qfc::attn_decode_cuda, "paged split-KV decode attention");
+  m.def("attn_prefill", &qfc::attn_prefill_cuda, "causal flash prefill attention (tcgen05)");
+  m.def("attn_status", &qfc::attn_status, py::arg("clear") = false);
 
   m.def("ar_plan", &qfc::ar_plan, "region sizes a quantized all-reduce call needs");
   m.def("quant_all_reduce", &qfc::quant_all_reduce, "fused quantized all-reduce over peer memory",

@@ -40,7 +40,8 @@ PRESETS = {
                                              "high_freq_factor": 4.0, "original_max_position_embeddings": 8192},
                                max_position=8192, tie_word_embeddings=True),
     # small shapes for tests
-    "tiny": LlamaConfig("tiny", 512, 1024, 2, 8, 4, 1024, head_dim=64, max_position=2048),
+    "tiny": LlamaConfig("tiny", 1024, 2048, 2, 8, 4, 1024, head_dim=128, max_position=2048),
+    "tiny-hd64": LlamaConfig("tiny-hd64", 512, 1024, 2, 8, 4, 1024, head_dim=64, max_position=2048),
     "tiny-mha": LlamaConfig("tiny-mha", 1024, 2048, 2, 8, 8, 2048, head_dim=128, max_position=2048),
 }
 

@@ -1,8 +1,8 @@
 """Attention operators: causal prefill over the fused qkv activation, paged decode.
 
-``prefill_attention`` runs the hand-written sm_100a kernel when the extension provides
-one (``_C.attn_prefill``); until then it uses torch's SDPA (flagged by
-``PREFILL_BACKEND``).  ``decode_attention`` reads the paged KV cache.
+``prefill_attention`` runs the tcgen05 flash kernel of ``csrc/attn_prefill.cu`` for bf16
+with head_dim 128 (every Llama configuration here); other head sizes fall back to torch's
+SDPA.  ``decode_attention`` runs the paged split-KV kernel of ``csrc/attn_decode.cu``.
 """
 from __future__ import annotations
 
@@ -11,20 +11,23 @@ import torch.nn.functional as F
 
 from .._ext import ext
 
-__all__ = ["prefill_attention", "decode_attention", "prefill_backend"]
+__all__ = ["prefill_attention", "decode_attention", "prefill_backend", "attn_status"]
 
 
-def prefill_backend() -> str:
-    return "qfc" if hasattr(ext(), "attn_prefill") else "sdpa"
+def _native(qkv: torch.Tensor, hd: int) -> bool:
+    return qkv.is_cuda and qkv.dtype == torch.bfloat16 and hd == 128
+
+
+def prefill_backend(hd: int = 128) -> str:
+    return "qfc-tcgen05" if hd == 128 else "sdpa"
 
 
 def prefill_attention(qkv: torch.Tensor, B: int, S: int, nq: int, nkv: int, hd: int,
                       out: torch.Tensor | None = None) -> torch.Tensor:
     """Causal self-attention of B sequences of length S; qkv [B*S, (nq+2nkv)*hd] -> [B*S, nq*hd]."""
-    C = ext()
-    if hasattr(C, "attn_prefill"):
+    if _native(qkv, hd):
         o = torch.empty(B * S, nq * hd, dtype=qkv.dtype, device=qkv.device) if out is None else out
-        C.attn_prefill(qkv, o, B, S, nq, nkv, hd, 1.0 / hd ** 0.5)
+        ext().attn_prefill(qkv, o, B, S, nq, nkv, hd, 1.0 / hd ** 0.5)
         return o
     x = qkv.view(B, S, nq + 2 * nkv, hd)
     q = x[:, :, :nq].transpose(1, 2)
@@ -49,3 +52,8 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     o = torch.empty_like(q) if out is None else out
     ext().attn_decode(q, k_cache, v_cache, block_table, seq_lens, o, nq, nkv, hd, 1.0 / hd ** 0.5)
     return o
+
+
+def attn_status(clear: bool = False) -> int:
+    """Nonzero if the prefill attention kernel gave up waiting on a pipeline barrier."""
+    return int(ext().attn_status(clear))
