@@ -19,7 +19,7 @@ def _ref(qkv, B, S, nq, nkv, hd):
     return (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B * S, nq * hd)
 
 
-@pytest.mark.parametrize("B,S,nq,nkv", [(1, 128, 1, 1), (2, 100, 4, 4), (2, 300, 8, 2), (1, 1024, 4, 1),
+@pytest.mark.parametrize("B,S,nq,nkv", [(1, 128, 1, 1), (2, 100, 4, 4), (2, 300, 8, 2), (1, 1024, 4, 1), (3, 100, 8, 4),
                                          (3, 257, 2, 2), (8, 1024, 4, 4)])
 def test_prefill_attention_matches_reference(cuda_device, B, S, nq, nkv):
     hd = 128

@@ -16,7 +16,12 @@ def _hf(cfg, sd, dev):
               head_dim=cfg.head_dim, rms_norm_eps=cfg.rms_eps, rope_theta=cfg.rope_theta,
               max_position_embeddings=cfg.max_position, tie_word_embeddings=False)
     with torch.device(dev):
-        hf = LlamaForCausalLM(hfc).to(torch.bfloat16)
+        hf = LlamaForCausalLM(hfc)
+    # Cast parameters only: the rotary inverse-frequency buffers stay fp32, as after
+    # from_pretrained (a blanket .to(bfloat16) would round the rotation angles too).
+    dtype = next(iter(sd.values())).dtype
+    for p in hf.parameters():
+        p.data = p.data.to(dtype)
     missing, unexpected = hf.load_state_dict(sd, strict=False)
     assert not unexpected and all("rotary" in k for k in missing)
     return hf.eval()
