@@ -5,7 +5,8 @@
 // (after RoPE); V is first transposed into vt [B * nkv * hd, S_pad] so that both matrix
 // products read K-major operands with the same 128-byte-swizzled TMA layout as the GEMM.
 //
-// One CTA per (128-query tile, query head, sequence), 10 warps:
+// Persistent: one CTA per SM walks (128-query tile, query head, sequence) work items,
+// heaviest first; 10 warps:
 //   warp 0      TMA: Q once, then K_j and V^T_j into a 2-stage ring;
 //   warp 1      TMEM allocation and MMA issue: S_j = Q K_j^T (M=N=128, K=hd) into one of two
 //               TMEM S buffers, then O_j = P_j V_j (M=128, N=hd, K=128) into one of two
@@ -66,6 +67,18 @@ QFC_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" 
 // K-major tile of 64 bf16 columns: rows are 128 bytes, chunk index XOR (row mod 8).
 QFC_DEV uint32_t sw128_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
+// Work item i -> (query tile, head, sequence); heaviest (last) query tiles first.
+QFC_DEV void item_coords(int i, const Args& a, int& qt, int& h, int& b) {
+  const int per_tile = a.nq * a.B;
+  qt = a.q_tiles - 1 - i / per_tile;
+  const int r = i % per_tile;
+  h = r % a.nq;
+  b = r / a.nq;
+}
+
+// Persistent: each CTA walks work items blockIdx.x, +gridDim.x, ...  Every role walks
+// the same items, and a global tile counter t (over all items of this CTA) selects the
+// ring slot (t & 1) and mbarrier phase ((t >> 1) & 1) of every double buffer.
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmVT,
                     const Args args) {
@@ -87,22 +100,21 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_cons
   uint64_t* o_empty = bars + 15;  // [2]
   uint64_t* drain = bars + 17;
   uint64_t* a_empty = bars + 18;  // [2] correction has read alpha / l of this buffer
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* q_empty = bars + 20;  // all QK MMAs of the current item are done with Q
+  uint64_t* v_full = bars + 21;   // [2] V^T tile landed (kv_full / kv_empty track K)
+  uint64_t* v_empty = bars + 23;  // [2] PV MMA done with V^T
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 25);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* s_alpha = reinterpret_cast<float*>(tmem_holder + 4);  // [2][128]
   float* s_l = s_alpha + 256;                                   // [2][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Heaviest (last) query tiles first.
-  const int qt = args.q_tiles - 1 - (int)blockIdx.x;
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int kvh = h / args.group;
-  const int q0 = qt * BQ;
-  const int n_kv = min(qt + 1, (args.S + BKV - 1) / BKV);  // causal: tiles 0..qt
-  const int row_base = b * args.S;
+  const int n_items = args.q_tiles * args.nq * args.B;
+  const int kv_tiles = (args.S + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
     tc::mbar_init(tc::smem_u32(q_full), 1);
+    tc::mbar_init(tc::smem_u32(q_empty), 1);
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(tc::smem_u32(&kv_full[i]), 1);
       tc::mbar_init(tc::smem_u32(&kv_empty[i]), 1);
@@ -113,6 +125,8 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_cons
       tc::mbar_init(tc::smem_u32(&o_full[i]), 1);
       tc::mbar_init(tc::smem_u32(&o_empty[i]), 128);
       tc::mbar_init(tc::smem_u32(&a_empty[i]), 128);
+      tc::mbar_init(tc::smem_u32(&v_full[i]), 1);
+      tc::mbar_init(tc::smem_u32(&v_empty[i]), 1);
     }
     tc::mbar_init(tc::smem_u32(drain), 1);
     *s_abort = 0;
@@ -126,89 +140,127 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_cons
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_holder;  // S[0]=+0, S[1]=+128, O[0]=+256, O[1]=+384
+  auto wait = [&](uint64_t* bar, uint32_t parity) {
+    return tc::mbar_wait(tc::smem_u32(bar), parity, globaltimer_ns() + args.timeout_ns, s_abort);
+  };
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       tc::tma_prefetch_desc(&tmQKV);
       tc::tma_prefetch_desc(&tmVT);
-      const uint32_t qb = tc::smem_u32(q_full);
-      tc::mbar_arrive_expect_tx(qb, TILE_BYTES);
-      tc::tma_load_2d(tc::smem_u32(sQ), &tmQKV, qb, h * HD, row_base + q0);
-      tc::tma_load_2d(tc::smem_u32(sQ + HALF_BYTES), &tmQKV, qb, h * HD + 64, row_base + q0);
-      int issued[2] = {-1, -1};
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (!tc::mbar_wait(tc::smem_u32(&kv_empty[st]), ((j >> 1) & 1) ^ 1, globaltimer_ns() + args.timeout_ns,
-                           s_abort)) {
-          fail(args, s_abort, 0x1001);
+      int t = 0, k = 0;
+      int issued[2] = {-1, -1}, v_issued[2] = {-1, -1}, q_issued = -1;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++k) {
+        int qt, h, b;
+        item_coords(item, args, qt, h, b);
+        const int kvh = h / args.group;
+        const int row_base = b * args.S;
+        const int n_kv = min(qt + 1, kv_tiles);
+        if (!wait(q_empty, (k & 1) ^ 1)) {
+          fail(args, s_abort, 0x1002);
           break;
         }
-        const uint32_t fb = tc::smem_u32(&kv_full[st]);
-        tc::mbar_arrive_expect_tx(fb, 2 * TILE_BYTES);
-        const int kcol = (args.nq + kvh) * HD;
-        tc::tma_load_2d(tc::smem_u32(sK + st * TILE_BYTES), &tmQKV, fb, kcol, row_base + j * BKV);
-        tc::tma_load_2d(tc::smem_u32(sK + st * TILE_BYTES + HALF_BYTES), &tmQKV, fb, kcol + 64, row_base + j * BKV);
-        const int vrow = (b * args.nkv + kvh) * HD;
-        tc::tma_load_2d(tc::smem_u32(sV + st * TILE_BYTES), &tmVT, fb, j * BKV, vrow);
-        tc::tma_load_2d(tc::smem_u32(sV + st * TILE_BYTES + HALF_BYTES), &tmVT, fb, j * BKV + 64, vrow);
-        issued[st] = j;
+        const uint32_t qb = tc::smem_u32(q_full);
+        tc::mbar_arrive_expect_tx(qb, TILE_BYTES);
+        tc::tma_load_2d(tc::smem_u32(sQ), &tmQKV, qb, h * HD, row_base + qt * BQ);
+        tc::tma_load_2d(tc::smem_u32(sQ + HALF_BYTES), &tmQKV, qb, h * HD + 64, row_base + qt * BQ);
+        q_issued = k;
+        for (int j = 0; j < n_kv; ++j, ++t) {
+          const int st = t & 1;
+          if (!wait(&kv_empty[st], ((t >> 1) & 1) ^ 1)) {
+            fail(args, s_abort, 0x1001);
+            ok = false;
+            break;
+          }
+          const uint32_t fb = tc::smem_u32(&kv_full[st]);
+          tc::mbar_arrive_expect_tx(fb, TILE_BYTES);
+          const int kcol = (args.nq + kvh) * HD;
+          tc::tma_load_2d(tc::smem_u32(sK + st * TILE_BYTES), &tmQKV, fb, kcol, row_base + j * BKV);
+          tc::tma_load_2d(tc::smem_u32(sK + st * TILE_BYTES + HALF_BYTES), &tmQKV, fb, kcol + 64, row_base + j * BKV);
+          issued[st] = t;
+          // V^T of this tile: its slot frees later (after PV), so it is loaded second
+          if (!wait(&v_empty[st], ((t >> 1) & 1) ^ 1)) {
+            fail(args, s_abort, 0x1003);
+            ok = false;
+            break;
+          }
+          const uint32_t vb = tc::smem_u32(&v_full[st]);
+          tc::mbar_arrive_expect_tx(vb, TILE_BYTES);
+          const int vrow = (b * args.nkv + kvh) * HD;
+          tc::tma_load_2d(tc::smem_u32(sV + st * TILE_BYTES), &tmVT, vb, j * BKV, vrow);
+          tc::tma_load_2d(tc::smem_u32(sV + st * TILE_BYTES + HALF_BYTES), &tmVT, vb, j * BKV + 64, vrow);
+          v_issued[st] = t;
+        }
       }
       if (*s_abort) {  // let issued copies land before shared memory goes away
         int never = 0;
-        tc::mbar_wait(qb, 0, globaltimer_ns() + 50000000ull, &never);
-        for (int st = 0; st < 2; ++st)
+        if (q_issued >= 0) tc::mbar_wait(tc::smem_u32(q_full), q_issued & 1, globaltimer_ns() + 50000000ull, &never);
+        for (int st = 0; st < 2; ++st) {
           if (issued[st] >= 0)
             tc::mbar_wait(tc::smem_u32(&kv_full[st]), (issued[st] >> 1) & 1, globaltimer_ns() + 50000000ull, &never);
+          if (v_issued[st] >= 0)
+            tc::mbar_wait(tc::smem_u32(&v_full[st]), (v_issued[st] >> 1) & 1, globaltimer_ns() + 50000000ull, &never);
+        }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      bool ok = tc::mbar_wait(tc::smem_u32(q_full), 0, globaltimer_ns() + args.timeout_ns, s_abort);
-      bool issued_any = false;
-      auto issue_qk = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!tc::mbar_wait(tc::smem_u32(&kv_full[st]), (j >> 1) & 1, globaltimer_ns() + args.timeout_ns, s_abort))
-          return false;
-        if (!tc::mbar_wait(tc::smem_u32(&s_empty[st]), ((j >> 1) & 1) ^ 1, globaltimer_ns() + args.timeout_ns, s_abort))
-          return false;
+      bool ok = true, issued_any = false;
+      int t = 0, k = 0;
+      auto issue_qk = [&](int tt) -> bool {
+        const int st = tt & 1;
+        if (!wait(&kv_full[st], (tt >> 1) & 1) || !wait(&s_empty[st], ((tt >> 1) & 1) ^ 1)) return false;
         tc::tc_fence_after();
         const uint32_t a0 = tc::smem_u32(sQ), b0 = tc::smem_u32(sK + st * TILE_BYTES);
 #pragma unroll
         for (int s = 0; s < 2; ++s)
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            tc::umma_f16(tmem + st * 128, tc::sw128_kmajor_desc(a0 + s * HALF_BYTES + k * 32),
-                         tc::sw128_kmajor_desc(b0 + s * HALF_BYTES + k * 32), IDESC, (s | k) != 0);
+          for (int kk = 0; kk < 4; ++kk)
+            tc::umma_f16(tmem + st * 128, tc::sw128_kmajor_desc(a0 + s * HALF_BYTES + kk * 32),
+                         tc::sw128_kmajor_desc(b0 + s * HALF_BYTES + kk * 32), IDESC, (s | kk) != 0);
         tc::umma_commit(tc::smem_u32(&s_full[st]));
+        tc::umma_commit(tc::smem_u32(&kv_empty[st]));  // K slot free once this QK is done
         issued_any = true;
         return true;
       };
-      if (ok) ok = issue_qk(0);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j & 1;
-        if (j + 1 < n_kv && !issue_qk(j + 1)) {
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++k) {
+        int qt, h, b;
+        item_coords(item, args, qt, h, b);
+        const int n_kv = min(qt + 1, kv_tiles);
+        if (!wait(q_full, k & 1) || !issue_qk(t)) {
           ok = false;
           break;
         }
-        if (!tc::mbar_wait(tc::smem_u32(&p_full[st]), (j >> 1) & 1, globaltimer_ns() + args.timeout_ns, s_abort) ||
-            !tc::mbar_wait(tc::smem_u32(&o_empty[st]), ((j >> 1) & 1) ^ 1, globaltimer_ns() + args.timeout_ns,
-                           s_abort)) {
-          ok = false;
-          break;
+        for (int j = 0; j < n_kv; ++j, ++t) {
+          const int st = t & 1;
+          if (j + 1 < n_kv) {
+            if (!issue_qk(t + 1)) {
+              ok = false;
+              break;
+            }
+          } else {
+            tc::umma_commit(tc::smem_u32(q_empty));  // Q free once this item's QK MMAs are done
+          }
+          if (!wait(&p_full[st], (t >> 1) & 1) || !wait(&o_empty[st], ((t >> 1) & 1) ^ 1) ||
+              !wait(&v_full[st], (t >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t a0 = tc::smem_u32(sP + st * TILE_BYTES), b0 = tc::smem_u32(sV + st * TILE_BYTES);
+#pragma unroll
+          for (int s = 0; s < 2; ++s)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc::umma_f16(tmem + 256 + st * 128, tc::sw128_kmajor_desc(a0 + s * HALF_BYTES + kk * 32),
+                           tc::sw128_kmajor_desc(b0 + s * HALF_BYTES + kk * 32), IDESC, (s | kk) != 0);
+          tc::umma_commit(tc::smem_u32(&o_full[st]));
+          tc::umma_commit(tc::smem_u32(&p_empty[st]));
+          tc::umma_commit(tc::smem_u32(&v_empty[st]));
         }
-        tc::tc_fence_after();
-        const uint32_t a0 = tc::smem_u32(sP + st * TILE_BYTES), b0 = tc::smem_u32(sV + st * TILE_BYTES);
-#pragma unroll
-        for (int s = 0; s < 2; ++s)
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            tc::umma_f16(tmem + 256 + st * 128, tc::sw128_kmajor_desc(a0 + s * HALF_BYTES + k * 32),
-                         tc::sw128_kmajor_desc(b0 + s * HALF_BYTES + k * 32), IDESC, (s | k) != 0);
-        tc::umma_commit(tc::smem_u32(&o_full[st]));
-        tc::umma_commit(tc::smem_u32(&p_empty[st]));
-        tc::umma_commit(tc::smem_u32(&kv_empty[st]));
       }
       if (!ok) fail(args, s_abort, 0x2001);
       if ((!ok || *s_abort) && issued_any) {
@@ -220,111 +272,127 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_cons
   } else if (warp < 6) {
     // ---------------------------------------------------------------- softmax
     const int r = (warp & 3) * 32 + lane;  // query row in the tile (= TMEM lane)
-    const int qpos = q0 + r;
-    float m = -INFINITY, l = 0.f;
-    for (int j = 0; j < n_kv; ++j) {
-      const int st = j & 1;
-      if (!tc::mbar_wait(tc::smem_u32(&s_full[st]), (j >> 1) & 1, globaltimer_ns() + args.timeout_ns, s_abort)) {
-        fail(args, s_abort, 0x3001);
-        break;
-      }
-      tc::tc_fence_after();
-      float sv[128];
-      const uint32_t ta = tmem + st * 128 + ((uint32_t)((warp & 3) * 32) << 16);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t u[32];
-        tc::tmem_ld_32x32b_x32(ta + c * 32, u);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[i]);
-      }
-      tc::tc_fence_before();
-      tc::mbar_arrive(tc::smem_u32(&s_empty[st]));
-      // masks: keys above the diagonal and keys past the end of the sequence
-      const int k0 = j * BKV;
-      const int kmax = min(qpos, args.S - 1) - k0;  // last visible column (may be < 0 or >= 127)
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        sv[i] = (i <= kmax) ? sv[i] * args.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, sv[i]);
-      }
-      const float m_new = fmaxf(m, mx);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = ex2(m - m_use);
-      // P buffer st is free once PV(j-2) finished reading it
-      if (!tc::mbar_wait(tc::smem_u32(&p_empty[st]), ((j >> 1) & 1) ^ 1, globaltimer_ns() + args.timeout_ns,
-                         s_abort)) {
-        fail(args, s_abort, 0x3002);
-        break;
-      }
-      float sum = 0.f;
-      uint8_t* pbase = sP + st * TILE_BYTES;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 keys
-        uint32_t w[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float p0 = ex2(sv[c * 8 + 2 * t] - m_use);
-          const float p1 = ex2(sv[c * 8 + 2 * t + 1] - m_use);
-          sum += p0 + p1;
-          w[t] = pack_bf16x2(p0, p1);
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    int t = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      int qt, h, b;
+      item_coords(item, args, qt, h, b);
+      const int n_kv = min(qt + 1, kv_tiles);
+      const int qpos = qt * BQ + r;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n_kv; ++j, ++t) {
+        const int st = t & 1;
+        if (!wait(&s_full[st], (t >> 1) & 1)) {
+          fail(args, s_abort, 0x3001);
+          ok = false;
+          break;
         }
-        uint8_t* dst = pbase + (c >> 3) * HALF_BYTES + sw128_off(r, c & 7);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        tc::tc_fence_after();
+        float sv[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t u[32];
+          tc::tmem_ld_32x32b_x32(tmem + st * 128 + lane_off + c * 32, u);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[i]);
+        }
+        tc::tmem_wait_ld();
+        tc::tc_fence_before();
+        tc::mbar_arrive(tc::smem_u32(&s_empty[st]));
+        // columns past kmax are masked: keys above the diagonal or past the sequence end
+        const int kmax = min(qpos, args.S - 1) - j * BKV;
+        if (kmax < BKV - 1) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i) sv[i] = (i <= kmax) ? sv[i] : -INFINITY;
+        }
+        float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+        for (int i = 4; i < 128; i += 4) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) mx4[q] = fmaxf(mx4[q], sv[i + q]);
+        }
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * args.scale_log2;
+        const float m_new = fmaxf(m, mx);
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+        const float alpha = ex2(m - m_use);
+        // P buffer st is free once PV(t-2) finished reading it
+        if (!wait(&p_empty[st], ((t >> 1) & 1) ^ 1)) {
+          fail(args, s_abort, 0x3002);
+          ok = false;
+          break;
+        }
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+        uint8_t* pbase = sP + st * TILE_BYTES;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 keys
+          uint32_t w[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float p0 = ex2(fmaf(sv[c * 8 + 2 * q], args.scale_log2, -m_use));
+            const float p1 = ex2(fmaf(sv[c * 8 + 2 * q + 1], args.scale_log2, -m_use));
+            sum4[q] += p0 + p1;
+            w[q] = pack_bf16x2(p0, p1);
+          }
+          uint8_t* dst = pbase + (c >> 3) * HALF_BYTES + sw128_off(r, c & 7);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        fence_async_smem();
+        // alpha / l buffer st is free once the correction thread has read tile t-2's
+        if (!wait(&a_empty[st], ((t >> 1) & 1) ^ 1)) {
+          fail(args, s_abort, 0x3003);
+          ok = false;
+          break;
+        }
+        l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+        m = m_new;
+        s_alpha[st * 128 + r] = alpha;
+        s_l[st * 128 + r] = l;
+        tc::mbar_arrive(tc::smem_u32(&p_full[st]));
       }
-      fence_async_smem();
-      // alpha / l buffer st is free once the correction thread has read tile j-2's
-      if (!tc::mbar_wait(tc::smem_u32(&a_empty[st]), ((j >> 1) & 1) ^ 1, globaltimer_ns() + args.timeout_ns,
-                         s_abort)) {
-        fail(args, s_abort, 0x3003);
-        break;
-      }
-      l = l * alpha + sum;
-      m = m_new;
-      s_alpha[st * 128 + r] = alpha;
-      s_l[st * 128 + r] = l;
-      tc::mbar_arrive(tc::smem_u32(&p_full[st]));
     }
   } else {
     // ---------------------------------------------------------------- correction / output
     const int r = (warp & 3) * 32 + lane;
-    float o[HD];
-#pragma unroll
-    for (int i = 0; i < HD; ++i) o[i] = 0.f;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    int t = 0;
     bool ok = true;
-    float l_final = 1.f;
-    for (int j = 0; j < n_kv; ++j) {
-      const int st = j & 1;
-      if (!tc::mbar_wait(tc::smem_u32(&p_full[st]), (j >> 1) & 1, globaltimer_ns() + args.timeout_ns, s_abort) ||
-          !tc::mbar_wait(tc::smem_u32(&o_full[st]), (j >> 1) & 1, globaltimer_ns() + args.timeout_ns, s_abort)) {
-        fail(args, s_abort, 0x4001);
-        ok = false;
-        break;
-      }
-      tc::tc_fence_after();
-      const float alpha = s_alpha[st * 128 + r];
-      l_final = s_l[st * 128 + r];
-      tc::mbar_arrive(tc::smem_u32(&a_empty[st]));
-      const uint32_t ta = tmem + 256 + st * 128 + ((uint32_t)((warp & 3) * 32) << 16);
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      int qt, h, b;
+      item_coords(item, args, qt, h, b);
+      const int n_kv = min(qt + 1, kv_tiles);
+      float o[HD];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t u[32];
-        tc::tmem_ld_32x32b_x32(ta + c * 32, u);
-        tc::tmem_wait_ld();
+      for (int i = 0; i < HD; ++i) o[i] = 0.f;
+      float l_final = 1.f;
+      for (int j = 0; j < n_kv; ++j, ++t) {
+        const int st = t & 1;
+        if (!wait(&p_full[st], (t >> 1) & 1) || !wait(&o_full[st], (t >> 1) & 1)) {
+          fail(args, s_abort, 0x4001);
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const float alpha = s_alpha[st * 128 + r];
+        l_final = s_l[st * 128 + r];
+        tc::mbar_arrive(tc::smem_u32(&a_empty[st]));
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha + __uint_as_float(u[i]);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t u[32];
+          tc::tmem_ld_32x32b_x32(tmem + 256 + st * 128 + lane_off + c * 32, u);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha, __uint_as_float(u[i]));
+        }
+        tc::tc_fence_before();
+        tc::mbar_arrive(tc::smem_u32(&o_empty[st]));
       }
-      tc::tc_fence_before();
-      tc::mbar_arrive(tc::smem_u32(&o_empty[st]));
-    }
-    // l_final was written by this row's softmax thread before its last p_full arrival
-    if (ok && !*s_abort) {
-      const int qpos = q0 + r;
+      // l_final was written by this row's softmax thread before its last p_full arrival
+      if (!ok || *s_abort) break;
+      const int qpos = qt * BQ + r;
       if (qpos < args.S) {
         const float inv = 1.f / l_final;
-        __nv_bfloat16* dst = args.out + (int64_t)(row_base + qpos) * (args.nq * HD) + h * HD;
+        __nv_bfloat16* dst = args.out + (int64_t)(b * args.S + qpos) * (args.nq * HD) + h * HD;
 #pragma unroll
         for (int c = 0; c < HD / 8; ++c) {
           const uint4 v = make_uint4(pack_bf16x2(o[8 * c] * inv, o[8 * c + 1] * inv),
@@ -442,7 +510,10 @@ void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.status = status_word();
   a.timeout_ns = 10000000000ull;
-  dim3 grid((unsigned)a.q_tiles, (unsigned)nq, (unsigned)B);
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t items = (int64_t)a.q_tiles * nq * B;
+  const int grid = (int)std::min<int64_t>(items, sms);
   attn_prefill_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tq, tv, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
