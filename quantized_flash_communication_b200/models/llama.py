@@ -321,6 +321,53 @@ class LlamaTP(nn.Module):
         return self._head(x)
 
     @torch.no_grad()
+    def capture_prefill(self, batch: int, seq: int, cache: Optional[KVCache] = None,
+                        warmup: int = 2) -> "GraphedStep":
+        """Capture one prefill of ``[batch, seq]`` tokens as a CUDA graph.
+
+        Every kernel of the step (GEMMs, attention, the fused all-reduces, the head) is
+        replayed with one launch; all ranks of a tensor-parallel group must capture
+        together.  Returns a callable taking token ids and returning next tokens.
+        """
+        cache = cache if cache is not None else self.new_cache(batch, seq)
+        ids = torch.zeros(batch, seq, dtype=torch.int64, device=self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.prefill(ids, cache)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = self.prefill(ids, cache)
+        return GraphedStep(graph, ids, out)
+
+    @torch.no_grad()
+    def capture_decode(self, cache: KVCache, warmup: int = 2) -> "GraphedStep":
+        """Capture one decode step (one token per sequence) as a CUDA graph.
+
+        The graph reads positions from ``cache.seq_lens`` on the device, so the same graph
+        serves every step; the caller must not exceed the cache's capacity.
+        """
+        B = cache.seq_lens.numel()
+        tok = torch.zeros(B, dtype=torch.int64, device=self.device)
+        saved = cache.seq_lens.clone()
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.decode_step(tok, cache)
+                cache.seq_lens.copy_(saved)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = self.decode_step(tok, cache)
+        cache.seq_lens.copy_(saved)  # capture does not run the kernels, but keep state explicit
+        return GraphedStep(graph, tok, out)
+
+    @torch.no_grad()
     def generate(self, ids: torch.Tensor, max_new_tokens: int, cache: Optional[KVCache] = None) -> torch.Tensor:
         """Greedy generation; returns [B, max_new_tokens] new tokens."""
         B, S = ids.shape
@@ -333,6 +380,24 @@ class LlamaTP(nn.Module):
             tok = self.decode_step(tok, cache)
             out[:, t] = tok
         return out
+
+
+class GraphedStep:
+    """A captured model step: copy inputs into the static buffer, replay, read the output."""
+
+    def __init__(self, graph, inp: torch.Tensor, out: torch.Tensor):
+        self.graph = graph
+        self.inp = inp
+        self.out = out
+
+    def __call__(self, x: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x is not None:
+            self.inp.copy_(x.view_as(self.inp), non_blocking=True)
+        self.graph.replay()
+        return self.out
+
+    def release(self):
+        self.graph.reset()
 
 
 def smoke_forward(device) -> None:

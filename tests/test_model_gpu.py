@@ -94,3 +94,23 @@ def test_ultimate_tp_mlp_single_rank(cuda_device):
     y = mlp(x)
     ref = mlp.down_proj(torch.nn.functional.silu(mlp.gate_proj(x)) * mlp.up_proj(x))
     assert rel_l2(y.float(), ref.float()) < 0.02
+
+
+def test_cuda_graph_prefill_and_decode_match_eager(cuda_device):
+    cfg = get_config("tiny")
+    m = LlamaTP(cfg, TPContext(device=cuda_device), cuda_device, init="full", seed=4)
+    B, S = 2, 96
+    ids = torch.randint(0, cfg.vocab_size, (B, S), device=cuda_device)
+    c1 = m.new_cache(B, S + 3)
+    t_eager = m.prefill(ids, c1)
+    d_eager = m.decode_step(t_eager, c1)
+    c2 = m.new_cache(B, S + 3)
+    g = m.capture_prefill(B, S, c2)
+    t_graph = g(ids).clone()
+    assert torch.equal(t_graph, t_eager)
+    dg = m.capture_decode(c2)
+    assert int(c2.seq_lens[0]) == S
+    d_graph = dg(t_graph).clone()
+    assert torch.equal(d_graph, d_eager) and int(c2.seq_lens[0]) == S + 1
+    g.release()
+    dg.release()
