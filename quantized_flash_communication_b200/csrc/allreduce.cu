@@ -2,6 +2,7 @@
 // The kernels are in allreduce.cuh and are instantiated per input dtype in
 // allreduce_inst_*.cu (compiled in parallel).
 #include "allreduce.cuh"
+#include "scatter.h"
 
 namespace qfc {
 namespace ar {
@@ -13,7 +14,12 @@ QFC_AR_DECL(__half, __half)
 QFC_AR_DECL(float, float)
 QFC_AR_DECL(float, __half)
 #undef QFC_AR_DECL
+extern template void dispatch_gemm_reduce<__nv_bfloat16, __nv_bfloat16>(const ARParams&, const Plan&, int64_t, int,
+                                                                        cudaStream_t);
 }  // namespace ar
+
+// gemm.cu
+void gemm_qscatter(const at::Tensor& a, const at::Tensor& b, const ScatterArgs& sc, int p_bits, double timeout_ms);
 
 using namespace ar;
 
@@ -108,6 +114,69 @@ void quant_all_reduce(const std::vector<WsPtr>& wss, const std::vector<at::Tenso
   else if (in_dt == at::kFloat && out_dt == at::kFloat) go(float(), float());
   else if (in_dt == at::kFloat && out_dt == at::kHalf) go(float(), __half());
   else TORCH_CHECK(false, "quant_all_reduce: unsupported (input, output) dtype pair ", in_dt, ", ", out_dt);
+}
+
+// out = all_reduce(a @ w^T) over the workspace's ranks, with the quantize-and-scatter of the
+// two-shot all-reduce fused into the GEMM epilogue (one GEMM launch + one reduce-gather
+// launch).  a [M, K], w [N, K] bf16; out [M, N] bf16.  Group size 128, bits 16/8/6/4.
+void gemm_all_reduce(const WsPtr& ws, const at::Tensor& a, const at::Tensor& w, at::Tensor& out, int64_t bits,
+                     int64_t gs, bool sym, bool scale_fp32, double timeout_ms) {
+  TORCH_CHECK(gs == 128, "gemm_all_reduce: group size 128 only");
+  TORCH_CHECK(ws->peers_ready(), "gemm_all_reduce: workspace peers not mapped");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.is_contiguous(), "gemm_all_reduce: bf16 out");
+  const int64_t M = a.size(0), N = w.size(0);
+  TORCH_CHECK(out.numel() == M * N, "gemm_all_reduce: bad output size");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "gemm_all_reduce: out must be 16-byte aligned");
+  const int64_t n = M * N;
+  if (n == 0) return;
+  c10::cuda::CUDAGuard guard(a.device());
+  const int dev = a.get_device();
+  const int W = (int)ws->world();
+  const Plan pl = make_plan(n, W, (int)bits, (int)gs, scale_fp32, 2, false);
+  TORCH_CHECK(pl.need_rs <= ws->rs_bytes() && pl.need_ag <= ws->ag_bytes(),
+              "gemm_all_reduce: workspace too small for this message (grow it first)");
+  ScatterArgs sc;
+  std::memset(&sc, 0, sizeof(sc));
+  for (int r = 0; r < W; ++r) sc.base[r] = ws->peer_base(r);
+  sc.rs_off = ws->rs_off();
+  sc.slot1 = pl.slot1;
+  sc.pay1 = pl.pay1;
+  sc.chunk = pl.chunk;
+  sc.rank = (int)ws->rank();
+  sc.world = W;
+  sc.gs_shift = 7;
+  sc.sym = sym ? 1 : 0;
+  sc.meta_fp32 = scale_fp32 ? 1 : 0;
+  sc.epoch = ws->epochs() + ALG_GEMM_RS * kMaxBlocks + 0;
+  sc.done_ctas = ws->epochs() + ALG_GEMM_RS * kMaxBlocks + 1;
+  gemm_qscatter(a, w, sc, pl.p1, timeout_ms);
+  ARParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  for (int r = 0; r < W; ++r) prm.base[r] = ws->peer_base(r);
+  const int rk = (int)ws->rank();
+  prm.out[rk] = out.data_ptr();
+  prm.epochs[rk] = ws->epochs();
+  prm.gemm_epoch = sc.epoch;
+  prm.status = ws->status_dev();
+  prm.n = n;
+  prm.chunk = pl.chunk;
+  prm.rs_off = ws->rs_off();
+  prm.ag_off = ws->ag_off();
+  prm.os_off = ws->os_off();
+  prm.os_bytes = ws->os_bytes();
+  prm.slot1 = pl.slot1;
+  prm.slot2 = pl.slot2;
+  prm.pay1 = pl.pay1;
+  prm.pay2 = pl.pay2;
+  prm.timeout_ns = (uint64_t)(timeout_ms * 1e6);
+  prm.world = W;
+  prm.rank = rk;
+  prm.gs = (int)gs;
+  prm.gs_shift = 7;
+  prm.meta_fp32 = scale_fp32 ? 1 : 0;
+  prm.sym = sym ? 1 : 0;
+  prm.quantize_local = 1;
+  dispatch_gemm_reduce<__nv_bfloat16, __nv_bfloat16>(prm, pl, pl.chunk >> 8, dev, at::cuda::getCurrentCUDAStream());
 }
 
 }  // namespace qfc

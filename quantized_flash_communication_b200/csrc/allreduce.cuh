@@ -47,6 +47,7 @@ struct ARParams {
   char* base[kMaxRanks];
   uint32_t* epochs[kMaxRanks];
   KernelStatus* status;
+  uint32_t* gemm_epoch;  // FROM_GEMM: this rank's fused-GEMM epoch counter (device)
   int64_t n;       // elements
   int64_t chunk;   // two-shot: elements per chunk; one-shot: n rounded up to 256
   int64_t rs_off, ag_off, os_off, os_bytes;
@@ -265,7 +266,10 @@ QFC_DEV void split_item(int64_t item, int W, int64_t& i, int& jj) {
   }
 }
 
-template <typename InT, typename OutT, int P1, int P2, int WC>
+// FROM_GEMM: phase 1 was done by the row-parallel GEMM's epilogue (gemm.cu, EPI_QS*), which
+// stored every tile straight into its owner's reduce-scatter slot; this kernel waits for
+// the per-rank epoch flag each rank's GEMM published, then runs phases 2 and 3.
+template <typename InT, typename OutT, int P1, int P2, int WC, bool FROM_GEMM = false>
 __global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ ARParams p) {
   const int rank = gridDim.y > 1 ? (int)blockIdx.y : p.rank;
   const int W = WC > 0 ? WC : p.world;
@@ -295,7 +299,10 @@ __global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ A
 
   // Phase 1: quantize every chunk's units of this warp, push them to the chunk's owner.
   // Items (unit i, chunk jj), kBatch loads issued before the first is used.
-  {
+  if constexpr (FROM_GEMM) {
+    const uint32_t eg = *p.gemm_epoch;  // advanced by this rank's GEMM, which ran before
+    if (!wait_sources(p, my, PH_GEMM, 0, rank, W, eg, false, &s_abort)) return;
+  } else {
     const int64_t items = my_units * W;
     for (int64_t it = 0; it < items; it += kBatch) {
       Raw8<InT> raw[kBatch];
@@ -326,9 +333,11 @@ __global__ void __launch_bounds__(512) two_shot_kernel(const __grid_constant__ A
       }
     }
   }
-  __syncthreads();
-  if ((int)threadIdx.x < W) st_release_sys(flag_at(p.base[threadIdx.x], PH_RS, b, rank), e);
-  if (!wait_sources(p, my, PH_RS, b, rank, W, e, false, &s_abort)) return;
+  if constexpr (!FROM_GEMM) {
+    __syncthreads();
+    if ((int)threadIdx.x < W) st_release_sys(flag_at(p.base[threadIdx.x], PH_RS, b, rank), e);
+    if (!wait_sources(p, my, PH_RS, b, rank, W, e, false, &s_abort)) return;
+  }
 
   // Phase 2: reduce the own chunk, requantize, push to every peer, write own output.
   // NU units per batch so that NU * W slot loads are in flight.
@@ -625,6 +634,25 @@ void dispatch_bits_w(const ARParams& prm, const Plan& pl, bool one_shot, int64_t
   else if (pl.p1 == 8) launch_ar(two_shot_kernel<InT, OutT, 8, 8, WC>, prm, units, W_emul, dev, st);
   else if (pl.p2 == 8) launch_ar(two_shot_kernel<InT, OutT, 4, 8, WC>, prm, units, W_emul, dev, st);
   else launch_ar(two_shot_kernel<InT, OutT, 4, 4, WC>, prm, units, W_emul, dev, st);
+}
+
+template <typename InT, typename OutT, int WC>
+void dispatch_gemm_reduce_w(const ARParams& prm, const Plan& pl, int64_t units, int dev, cudaStream_t st) {
+  if (pl.p1 == 16) launch_ar(two_shot_kernel<InT, OutT, 16, 16, WC, true>, prm, units, 1, dev, st);
+  else if (pl.p1 == 8) launch_ar(two_shot_kernel<InT, OutT, 8, 8, WC, true>, prm, units, 1, dev, st);
+  else if (pl.p2 == 8) launch_ar(two_shot_kernel<InT, OutT, 4, 8, WC, true>, prm, units, 1, dev, st);
+  else launch_ar(two_shot_kernel<InT, OutT, 4, 4, WC, true>, prm, units, 1, dev, st);
+}
+
+// Phases 2-3 after a fused quantize-and-scatter GEMM.
+template <typename InT, typename OutT>
+void dispatch_gemm_reduce(const ARParams& prm, const Plan& pl, int64_t units, int dev, cudaStream_t st) {
+  switch (prm.world) {
+    case 2: dispatch_gemm_reduce_w<InT, OutT, 2>(prm, pl, units, dev, st); break;
+    case 4: dispatch_gemm_reduce_w<InT, OutT, 4>(prm, pl, units, dev, st); break;
+    case 8: dispatch_gemm_reduce_w<InT, OutT, 8>(prm, pl, units, dev, st); break;
+    default: dispatch_gemm_reduce_w<InT, OutT, 0>(prm, pl, units, dev, st); break;
+  }
 }
 
 // World sizes 2, 4 and 8 get specialised kernels (static indices, batched reduce);

@@ -27,6 +27,8 @@ std::vector<int64_t> ar_plan(int64_t n, int64_t world, int64_t bits, int64_t gs,
 void quant_all_reduce(const std::vector<std::shared_ptr<Workspace>>& wss, const std::vector<at::Tensor>& ins,
                       const std::vector<at::Tensor>& outs, int64_t bits, int64_t gs, bool sym, bool scale_fp32,
                       bool one_shot, bool quantize_local, double timeout_ms);
+void gemm_all_reduce(const std::shared_ptr<Workspace>& ws, const at::Tensor& a, const at::Tensor& w, at::Tensor& out,
+                     int64_t bits, int64_t gs, bool sym, bool scale_fp32, double timeout_ms);
 // gemm.cu
 at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& out, int64_t epi,
                      const c10::optional<at::Tensor>& residual, double timeout_ms, int64_t max_ctas);
@@ -102,4 +104,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("workspaces"), py::arg("ins"), py::arg("outs"), py::arg("bits"), py::arg("group_size"),
         py::arg("sym"), py::arg("scale_fp32"), py::arg("one_shot"), py::arg("quantize_local"),
         py::arg("timeout_ms"));
+  m.def("gemm_all_reduce", &qfc::gemm_all_reduce,
+        "all_reduce(a @ w^T) with the quantize-and-scatter fused into the GEMM epilogue", py::arg("workspace"),
+        py::arg("a"), py::arg("w"), py::arg("out"), py::arg("bits"), py::arg("group_size"), py::arg("sym"),
+        py::arg("scale_fp32"), py::arg("timeout_ms"));
 }

@@ -17,6 +17,10 @@
 //                 and writes silu(gate) * up (the reference's act_fn(gate) * up,
 //                 model.py:32-34) as bf16 [M, I]
 //   EPI_RESIDUAL  D = acc + R (bf16), for the residual stream when no all-reduce follows
+//   EPI_QS*       quantize every 128-column group of the bf16-rounded tile and store codes +
+//                 (scale, zero) into the owning rank's reduce-scatter slot over NVLink: the
+//                 first phase of the two-shot all-reduce, overlapped with the GEMM.  The
+//                 last CTA publishes a per-rank epoch flag to every peer.
 // Every mbarrier wait is bounded (%globaltimer); on expiry the CTA records an error code,
 // drains its in-flight copies and MMAs (bounded), frees TMEM and returns.
 #include <ATen/ATen.h>
@@ -27,7 +31,10 @@
 
 #include <mutex>
 
+#include <cstring>
+
 #include "common.cuh"
+#include "scatter.h"
 #include "tcgen05.cuh"
 
 namespace qfc {
@@ -45,7 +52,11 @@ constexpr int GROUP_M = 16;
 constexpr uint32_t IDESC = tc::idesc_f16(BM, BN, true);
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
-enum Epi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_RESIDUAL = 2 };
+// EPI_QS8 / EPI_QS4 / EPI_QS16: quantize each 128-column group of the (bf16-rounded) tile
+// to INT8 / INT4 / raw bf16 and store it into the owner rank's reduce-scatter slot.
+enum Epi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_RESIDUAL = 2, EPI_QS8 = 3, EPI_QS4 = 4, EPI_QS16 = 5 };
+
+constexpr bool is_qs(int epi) { return epi == EPI_QS8 || epi == EPI_QS4 || epi == EPI_QS16; }
 
 enum : int { GEMM_ERR_PRODUCER = 0x100, GEMM_ERR_MMA = 0x200, GEMM_ERR_EPI = 0x300 };
 
@@ -61,7 +72,66 @@ struct GemmArgs {
   int ldr;
   int* status;
   uint64_t timeout_ns;
+  ScatterArgs sc;    // EPI_QS*
 };
+
+// Quantize 128 consecutive values of one row (held by this thread) and store the codes
+// plus the group's (scale, zero) into slot / meta.  P = 8, 4 or 16 (raw bf16).
+template <int P>
+QFC_DEV void qs_store_group(const float (&v)[128], char* slot, char* meta, int64_t local, const ScatterArgs& sc) {
+  if constexpr (P == 16) {
+    uint4* dst = reinterpret_cast<uint4*>(slot + local * 2);
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      dst[k] = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                          pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+  } else {
+    float mn4[4] = {v[0], v[1], v[2], v[3]}, mx4[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+    for (int i = 4; i < 128; i += 4)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        mn4[q] = fminf(mn4[q], v[i + q]);
+        mx4[q] = fmaxf(mx4[q], v[i + q]);
+      }
+    const float mn = fminf(fminf(mn4[0], mn4[1]), fminf(mn4[2], mn4[3]));
+    const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+    float s, inv, z;
+    if (sc.sym) QMath<P, true>::params(mn, mx, s, inv, z);
+    else QMath<P, false>::params(mn, mx, s, inv, z);
+    if constexpr (P == 8) {
+      uint4* dst = reinterpret_cast<uint4*>(slot + local);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {  // 16 codes per 16-byte store
+        uint32_t m0[8], m1[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          m0[i] = QMath<P, false>::codebits(v[16 * k + i], inv, z);
+          m1[i] = QMath<P, false>::codebits(v[16 * k + 8 + i], inv, z);
+        }
+        const uint2 a = codebits8_to_u2(m0), b = codebits8_to_u2(m1);
+        dst[k] = make_uint4(a.x, a.y, b.x, b.y);
+      }
+    } else {
+      uint4* dst = reinterpret_cast<uint4*>(slot + (local >> 1));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {  // 32 codes per 16-byte store
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t m[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) m[i] = QMath<P, false>::codebits(v[32 * k + 8 * q + i], inv, z);
+          w[q] = codebits8_to_int4(m);
+        }
+        dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    const int64_t g = local >> sc.gs_shift;
+    if (sc.meta_fp32) *reinterpret_cast<float2*>(meta + g * 8) = make_float2(s, z);
+    else *reinterpret_cast<uint32_t*>(meta + g * 4) = pack_f16x2(s, z);
+  }
+}
 
 QFC_DEV void tile_coords(int tile, int m_tiles, int n_tiles, int& mb, int& nb) {
   const int group = GROUP_M * n_tiles;
@@ -227,13 +297,40 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const uint32_t taddr = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
       const int row = mb * BM + row_in_tile;
       const int col0 = nb * args.n_tile_cols;
-      if constexpr (EPI == EPI_SWIGLU) {
+      if constexpr (is_qs(EPI)) {
+        constexpr int P = EPI == EPI_QS8 ? 8 : (EPI == EPI_QS4 ? 4 : 16);
+#pragma unroll 1
+        for (int g0 = 0; g0 < BN; g0 += 128) {  // two 128-column groups per tile
+          uint32_t r[4][32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tc::tmem_ld_32x32b_x32(taddr + g0 + c * 32, r[c]);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tc::tmem_reg_fence(r[c]);
+          const int col = col0 + g0;
+          if (row < args.M && col < args.N) {
+            float v[128];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+              for (int j = 0; j < 32; ++j)  // the bf16 value the unfused GEMM would have stored
+                v[c * 32 + j] = to_f32(from_f32<__nv_bfloat16>(__uint_as_float(r[c][j])));
+            const int64_t e = (int64_t)row * args.N + col;
+            const int owner = (int)(e / args.sc.chunk);
+            const int64_t local = e - (int64_t)owner * args.sc.chunk;
+            char* slot = args.sc.base[owner] + args.sc.rs_off + (int64_t)args.sc.rank * args.sc.slot1;
+            qs_store_group<P>(v, slot, slot + args.sc.pay1, local, args.sc);
+          }
+        }
+      } else if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll 1
         for (int c = 0; c < 128; c += 32) {
           uint32_t g[32], u[32];
           tc::tmem_ld_32x32b_x32(taddr + c, g);
           tc::tmem_ld_32x32b_x32(taddr + 128 + c, u);
           tc::tmem_wait_ld();
+          tc::tmem_reg_fence(g);
+          tc::tmem_reg_fence(u);
           const int col = col0 + c;
           if (row < args.M && col < args.N) {
             uint32_t o[16];
@@ -266,6 +363,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           uint32_t r[32];
           tc::tmem_ld_32x32b_x32(taddr + c, r);
           tc::tmem_wait_ld();
+          tc::tmem_reg_fence(r);
           const int col = col0 + c;
           if (row < args.M && col < args.N) {
             float v[32];
@@ -302,8 +400,29 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       tc::tc_fence_before();
       tc::mbar_arrive(tc::smem_u32(&tempty[buf]));
     }
+    // Peer stores of this thread are visible system-wide before the CTA reports done.
+    if constexpr (is_qs(EPI)) __threadfence_system();
   }
   __syncthreads();
+  if constexpr (is_qs(EPI)) {
+    // The last CTA to finish advances this rank's fused-GEMM epoch and publishes it to
+    // every rank: the reduce-scatter slots of all of this rank's tiles are filled.
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      const uint32_t prev = atomicAdd(args.sc.done_ctas, 1u);
+      if (prev == gridDim.x - 1) {
+        *args.sc.done_ctas = 0u;
+        const uint32_t e = *args.sc.epoch + 1u;
+        *args.sc.epoch = e;
+        __threadfence_system();
+        for (int j = 0; j < args.sc.world; ++j) {
+          uint32_t* flag = reinterpret_cast<uint32_t*>(args.sc.base[j]) +
+                           ((int64_t)(PH_GEMM * kMaxBlocks + 0) * kMaxRanks + args.sc.rank);
+          st_release_sys(flag, e);
+        }
+      }
+    }
+  }
   if (warp == 1) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem_base, TMEM_COLS);
@@ -362,8 +481,8 @@ int sm_count(int dev) {
 }
 
 template <int EPI>
-void launch(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const at::Tensor* R, int M, int N, int K,
-            double timeout_ms, int max_ctas) {
+void launch(const at::Tensor& A, const at::Tensor& B, at::Tensor* D, const at::Tensor* R, int M, int N, int K,
+            double timeout_ms, int max_ctas, const ScatterArgs* sc = nullptr) {
   static bool attr_set[64] = {false};
   const int dev = A.get_device();
   auto kern = gemm_bf16_kernel<EPI>;
@@ -385,8 +504,10 @@ void launch(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const at::T
     a.b_second = 128;
   }
   a.n_tiles = (N + a.n_tile_cols - 1) / a.n_tile_cols;
-  a.D = reinterpret_cast<__nv_bfloat16*>(D.data_ptr());
-  a.ldd = (int)D.stride(0);
+  a.D = D ? reinterpret_cast<__nv_bfloat16*>(D->data_ptr()) : nullptr;
+  a.ldd = D ? (int)D->stride(0) : 0;
+  std::memset(&a.sc, 0, sizeof(a.sc));
+  if (sc) a.sc = *sc;
   a.R = R ? reinterpret_cast<const __nv_bfloat16*>(R->data_ptr()) : nullptr;
   a.ldr = R ? (int)R->stride(0) : 0;
   a.status = status_word();
@@ -434,12 +555,32 @@ at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& b, const c10::option
     TORCH_CHECK(residual->size(0) == M && residual->size(1) == N, "gemm: bad residual shape");
   }
   switch (epi) {
-    case EPI_STORE: launch<EPI_STORE>(a, b, out, nullptr, M, N, K, timeout_ms, (int)max_ctas); break;
-    case EPI_SWIGLU: launch<EPI_SWIGLU>(a, b, out, nullptr, M, N, K, timeout_ms, (int)max_ctas); break;
-    case EPI_RESIDUAL: launch<EPI_RESIDUAL>(a, b, out, &*residual, M, N, K, timeout_ms, (int)max_ctas); break;
+    case EPI_STORE: launch<EPI_STORE>(a, b, &out, nullptr, M, N, K, timeout_ms, (int)max_ctas); break;
+    case EPI_SWIGLU: launch<EPI_SWIGLU>(a, b, &out, nullptr, M, N, K, timeout_ms, (int)max_ctas); break;
+    case EPI_RESIDUAL: launch<EPI_RESIDUAL>(a, b, &out, &*residual, M, N, K, timeout_ms, (int)max_ctas); break;
     default: TORCH_CHECK(false, "gemm: unknown epilogue ", epi);
   }
   return out;
+}
+
+// a @ b^T whose epilogue quantizes every 128-column group (p_bits 8 / 4, or 16 = raw
+// bf16) and stores it into the owner rank's reduce-scatter slot described by sc.
+void gemm_qscatter(const at::Tensor& a, const at::Tensor& b, const ScatterArgs& sc, int p_bits, double timeout_ms) {
+  using namespace gemm;
+  check_operand(a, "a");
+  check_operand(b, "b");
+  TORCH_CHECK(a.size(1) == b.size(1), "gemm: K mismatch");
+  const int M = (int)a.size(0), K = (int)a.size(1), N = (int)b.size(0);
+  TORCH_CHECK(N % 128 == 0 && sc.gs_shift == 7, "gemm_qscatter: group size 128 and N % 128 == 0 required");
+  TORCH_CHECK(sc.chunk % 256 == 0, "gemm_qscatter: chunk must be a multiple of 256");
+  c10::cuda::CUDAGuard guard(a.device());
+  if (M == 0) return;
+  switch (p_bits) {
+    case 8: launch<EPI_QS8>(a, b, nullptr, nullptr, M, N, K, timeout_ms, 0, &sc); break;
+    case 4: launch<EPI_QS4>(a, b, nullptr, nullptr, M, N, K, timeout_ms, 0, &sc); break;
+    case 16: launch<EPI_QS16>(a, b, nullptr, nullptr, M, N, K, timeout_ms, 0, &sc); break;
+    default: TORCH_CHECK(false, "gemm_qscatter: bits must be 8, 4 or 16");
+  }
 }
 
 // Error word of the GEMM kernels (0 = ok); clear = reset it to 0.

@@ -121,6 +121,14 @@ QFC_DEV void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 QFC_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// The registers written by tcgen05.ld are valid only after tcgen05.wait::ld, but the
+// compiler does not know that: this empty asm, placed after the wait, redefines them so
+// that no use can be scheduled above the wait.  Emits no instruction.
+QFC_DEV void tmem_reg_fence(uint32_t (&r)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 // Shared-memory matrix descriptor for a K-major tile written by TMA with 128-byte
 // swizzling: rows of 128 bytes (64 bf16), 8-row swizzle atoms of 1024 bytes stacked
 // along M/N (stride-dimension byte offset 1024).  The leading-dimension offset is not

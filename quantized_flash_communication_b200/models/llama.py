@@ -48,7 +48,7 @@ class TPContext:
     def __init__(self, group: Optional[dist.ProcessGroup] = None, device=None, ar_backend: str = "qfc",
                  bits: int = 8, group_size: int = 128, quant_type: str = "asym", algo: str = "auto",
                  reserve_tokens: int = 0, hidden_size: int = 0, world: Optional[int] = None,
-                 rank: Optional[int] = None):
+                 rank: Optional[int] = None, fuse_gemm: bool = True):
         self.group = group
         if world is not None:  # explicit (e.g. building one shard offline); no communication
             self.world, self.rank = world, rank or 0
@@ -64,6 +64,9 @@ class TPContext:
         self.group_size = group_size
         self.quant_type = quant_type
         self.algo = algo
+        # quantize-and-scatter inside the row-parallel GEMMs' epilogue (two-shot, group 128)
+        self.fuse_gemm = fuse_gemm and group_size == 128
+        self.fuse_min_rows = 256  # below this, messages go one-shot through the plain kernel
         self.ar: Optional[QuantAllReduce] = None
         if self.world > 1 and ar_backend == "qfc":
             self.ar = QuantAllReduce(group, self.device, bits=bits, group_size=group_size, quant_type=quant_type,
@@ -83,6 +86,14 @@ class TPContext:
             from ..parallel.staged import staged_all_reduce
             return staged_all_reduce(x, self.bits, self.group_size, self.quant_type, torch.float16, self.group, x.dtype)
         raise ValueError(f"unknown ar_backend {self.ar_backend!r}")
+
+    def linear_all_reduce(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """``all_reduce(x @ w.T)`` for a row-parallel layer (o_proj, down_proj)."""
+        if (self.world > 1 and self.ar_backend == "qfc" and self.fuse_gemm and x.shape[0] >= self.fuse_min_rows
+                and w.shape[0] % 128 == 0):
+            return self.ar.gemm_all_reduce(x, w)
+        p = G.linear(x, w)
+        return self.all_reduce(p, out=p)
 
     def gather_argmax(self, val: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
         """Global argmax from per-rank (max value, index) pairs; ties go to the lower index."""
@@ -251,16 +262,14 @@ class LlamaTP(nn.Module):
             G.linear_residual(o, lay.self_attn.o_proj.weight, h, out=h)
             x = L.rmsnorm(h, lay.post_attention_layernorm.weight, eps)
         else:
-            p = G.linear(o, lay.self_attn.o_proj.weight)
-            ar = tp.all_reduce(p, out=p)
+            ar = tp.linear_all_reduce(o, lay.self_attn.o_proj.weight)
             x = L.rmsnorm(ar, lay.post_attention_layernorm.weight, eps, residual=h)
         act = G.linear_swiglu(x, lay.mlp.gate_up_fused)
         nxt = (self.model.layers[li + 1].input_layernorm.weight if li + 1 < cfg.num_layers else self.model.norm.weight)
         if tp.world == 1:
             G.linear_residual(act, lay.mlp.down_proj.weight, h, out=h)
             return L.rmsnorm(h, nxt, eps)
-        p = G.linear(act, lay.mlp.down_proj.weight)
-        ar = tp.all_reduce(p, out=p)
+        ar = tp.linear_all_reduce(act, lay.mlp.down_proj.weight)
         return L.rmsnorm(ar, nxt, eps, residual=h)
 
     def _head(self, x_last: torch.Tensor) -> torch.Tensor:

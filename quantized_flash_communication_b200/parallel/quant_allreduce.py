@@ -119,6 +119,26 @@ class QuantAllReduce(_Base):
                                self.quantize_local, self.timeout_ms)
         return out
 
+    def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+                        bits: Optional[int] = None, quant_type: Optional[str] = None) -> torch.Tensor:
+        """``all_reduce(a @ w.T)`` with the two-shot reduce-scatter fused into the GEMM.
+
+        The tcgen05 GEMM's epilogue quantizes each 128-column group of its output tile and
+        stores it straight into the owning rank's reduce-scatter slot over NVLink, so the
+        transfer overlaps the remaining tiles; a second kernel then reduces, requantizes and
+        all-gathers.  Bit-identical to ``self(linear(a, w))`` with two-shot and group size 128.
+        """
+        bits = self.bits if bits is None else bits
+        qt = self.quant_type if quant_type is None else quant_type
+        a2 = a.reshape(-1, a.shape[-1])
+        M, N = a2.shape[0], w.shape[0]
+        if out is None:
+            out = torch.empty(*a.shape[:-1], N, dtype=torch.bfloat16, device=a.device)
+        fp32 = self.scale_dtype == torch.float32
+        self.ws.ensure(*self._plan(M * N, self.world, 2, bits, 128, fp32, False))
+        ext().gemm_all_reduce(self.ws.native, a2, w, out, bits, 128, qt == "sym", fp32, self.timeout_ms)
+        return out
+
     def check(self, synchronize: bool = True):
         self.ws.check(synchronize)
 

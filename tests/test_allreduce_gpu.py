@@ -123,6 +123,25 @@ def test_cuda_graph_replay(cuda_device):
             assert torch.equal(outs[r].cpu(), ref), it
 
 
+@pytest.mark.parametrize("bits,mode", [(8, "asym"), (4, "sym"), (6, "asym"), (16, "asym")])
+def test_gemm_fused_scatter_single_rank(cuda_device, bits, mode):
+    """GEMM with the quantize-and-scatter epilogue + reduce-gather == GEMM then all-reduce."""
+    from quantized_flash_communication_b200.ops import gemm as G
+    from quantized_flash_communication_b200.parallel import QuantAllReduce
+    ar = QuantAllReduce(None, cuda_device, bits=bits, group_size=128, quant_type=mode, algo="two_shot")
+    for M, K, N in [(256, 512, 1024), (1000, 1376, 4096), (130, 256, 384)]:
+        a = torch.randn(M, K, device=cuda_device, dtype=torch.bfloat16)
+        w = torch.randn(N, K, device=cuda_device, dtype=torch.bfloat16) * 0.05
+        for _ in range(2):
+            fused = ar.gemm_all_reduce(a, w)
+            ar.check()
+            plain = ar(G.linear(a, w))
+            ar.check()
+            assert torch.equal(fused, plain), (M, K, N)
+        ref = spec.two_step_all_reduce_ref([G.linear(a, w).cpu()], bits, 128, mode, torch.float16, torch.bfloat16)
+        assert torch.equal(fused.cpu(), ref)
+
+
 def test_timeout_reports_status_and_context_survives(cuda_device):
     """Rank 0 of a 2-rank workspace whose peer never runs: every wait must expire."""
     C = ext()

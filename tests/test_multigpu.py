@@ -60,20 +60,46 @@ def _case_allreduce(rank, world):
     return res
 
 
+def _case_gemm_fused(rank, world):
+    from quantized_flash_communication_b200 import quantization as spec
+    from quantized_flash_communication_b200.ops import gemm as G
+    from quantized_flash_communication_b200.parallel import QuantAllReduce
+    dev = torch.device("cuda", rank)
+    res = {}
+    for bits in (8, 6, 16):
+        ar = QuantAllReduce(None, dev, bits=bits, group_size=128, algo="two_shot", timeout_ms=5000)
+        for M, K, N in [(512, 512, 4096), (300, 1376, 1024)]:
+            outs = []
+            for r in range(world):
+                g = torch.Generator().manual_seed(10 * r + M)
+                a = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+                w = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+                outs.append((a, w))
+            parts = [G.linear(a, w).cpu() for a, w in outs]  # every rank's partial, computed here
+            ref = spec.two_step_all_reduce_ref(parts, bits, 128, "asym", torch.float16, torch.bfloat16)
+            ok = True
+            for _ in range(2):
+                y = ar.gemm_all_reduce(*outs[rank])
+                ar.check()
+                ok = ok and torch.equal(y.cpu(), ref)
+            res[(bits, M, K, N)] = ok
+    return res
+
+
 def _case_model(rank, world):
     from quantized_flash_communication_b200.models.config import get_config
     from quantized_flash_communication_b200.models.llama import LlamaTP, TPContext
     from quantized_flash_communication_b200.quantization import rel_l2
     dev = torch.device("cuda", rank)
     cfg = get_config("tiny-mha")
-    ids = torch.randint(0, cfg.vocab_size, (2, 64), generator=torch.Generator().manual_seed(3)).to(dev)
+    ids = torch.randint(0, cfg.vocab_size, (4, 96), generator=torch.Generator().manual_seed(3)).to(dev)
     out = {}
     ref = LlamaTP(cfg, TPContext(device=dev, world=1), dev, init="full", seed=9)
     _, h1 = ref.prefill(ids, return_last_hidden=True)
     for bits in (16, 8):
         tp = TPContext(None, dev, ar_backend="qfc", bits=bits, group_size=128)
         m = LlamaTP(cfg, tp, dev, init="full", seed=9)
-        cache = m.new_cache(2, 80)
+        cache = m.new_cache(4, 100)
         tok, h = m.prefill(ids, cache, return_last_hidden=True)
         tok2 = m.decode_step(tok, cache)
         gathered = [torch.empty_like(h) for _ in range(world)]
@@ -130,6 +156,14 @@ def _run(case, world=WORLD):
 @need2
 def test_fused_allreduce_matches_oracle_on_every_rank():
     res = _run("_case_allreduce")
+    for rank, r in res.items():
+        for k, ok in r.items():
+            assert ok, (rank, k)
+
+
+@need2
+def test_gemm_fused_scatter_matches_oracle_on_every_rank():
+    res = _run("_case_gemm_fused")
     for rank, r in res.items():
         for k, ok in r.items():
             assert ok, (rank, k)
