@@ -44,6 +44,8 @@ def _parse():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch kernels eagerly instead of one CUDA graph")
+    ap.add_argument("--no-fuse-gemm", action="store_true",
+                    help="run o_proj/down_proj GEMMs and the all-reduce as separate kernels")
     return ap.parse_args()
 
 
@@ -141,7 +143,8 @@ def run_ours(args):
     cfg = get_config(args.model)
     B, S = args.batch, args.seq
     tp = TPContext(None, dev, ar_backend=args.ar_backend, bits=args.bits, group_size=args.group_size,
-                   quant_type=args.quant_type, algo="auto", reserve_tokens=B * S, hidden_size=cfg.hidden_size)
+                   quant_type=args.quant_type, algo="auto", reserve_tokens=B * S, hidden_size=cfg.hidden_size,
+                   fuse_gemm=not args.no_fuse_gemm)
     model = LlamaTP(cfg, tp, dev, init="shard", seed=1234)
     g = torch.Generator(device="cpu").manual_seed(42)
     ids_host = torch.randint(0, cfg.vocab_size, (B, S), generator=g).pin_memory()
@@ -203,7 +206,8 @@ def run_ours(args):
         "dtype": "bf16",
         "data": "synthetic: uniform random token ids, random-init N(0,0.02) weights",
         "config": {"model": cfg.name, "global_batch": B, "seq_len": S, "parallelism": f"tp{world}",
-                   "allreduce": (f"qfc fused INT{args.bits} g{args.group_size} {args.quant_type}"
+                   "allreduce": (f"qfc INT{args.bits} g{args.group_size} {args.quant_type}"
+                                 + (", scatter fused into o/down GEMM epilogues" if tp.fuse_gemm else "")
                                  if args.ar_backend == "qfc" else args.ar_backend) if world > 1 else "none (tp1)",
                    "attention": A.prefill_backend(),
                    "launch": "cuda_graph" if graphed is not None else "eager",
