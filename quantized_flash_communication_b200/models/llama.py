@@ -74,11 +74,30 @@ class TPContext:
             if reserve_tokens and hidden_size:
                 self.ar.reserve(reserve_tokens * hidden_size, torch.bfloat16, bits_options=(bits, 16))
 
+    def configure(self, bits: Optional[int] = None, group_size: Optional[int] = None,
+                  quant_type: Optional[str] = None, backend: Optional[str] = None):
+        """Change the all-reduce settings at run time (the reference mutates ``mode``, ``bits``,
+        ``group_size`` and ``quant_type`` of every layer, main.py:93-97, 166-170)."""
+        if bits is not None:
+            self.bits = bits
+        if group_size is not None:
+            self.group_size = group_size
+        if quant_type is not None:
+            self.quant_type = quant_type
+        if backend is not None:
+            if backend == "qfc" and self.ar is None and self.world > 1:
+                self.ar = QuantAllReduce(self.group, self.device, bits=self.bits, group_size=128,
+                                         quant_type=self.quant_type, algo=self.algo)
+            self.ar_backend = backend
+
     def all_reduce(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self.world == 1:
             return x
-        if self.ar_backend == "qfc":
-            return self.ar(x, out=out)
+        if self.ar_backend == "qfc" and 8 <= self.group_size <= 256:
+            return self.ar(x, out=out, bits=self.bits, group_size=self.group_size, quant_type=self.quant_type)
+        if self.ar_backend == "qfc":  # groups above 256: the staged (torch.distributed) path
+            from ..parallel.staged import staged_all_reduce
+            return staged_all_reduce(x, self.bits, self.group_size, self.quant_type, torch.float16, self.group, x.dtype)
         if self.ar_backend == "nccl":
             dist.all_reduce(x, group=self.group)
             return x
@@ -89,9 +108,9 @@ class TPContext:
 
     def linear_all_reduce(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """``all_reduce(x @ w.T)`` for a row-parallel layer (o_proj, down_proj)."""
-        if (self.world > 1 and self.ar_backend == "qfc" and self.fuse_gemm and x.shape[0] >= self.fuse_min_rows
-                and w.shape[0] % 128 == 0):
-            return self.ar.gemm_all_reduce(x, w)
+        if (self.world > 1 and self.ar_backend == "qfc" and self.fuse_gemm and self.group_size == 128
+                and x.shape[0] >= self.fuse_min_rows and w.shape[0] % 128 == 0):
+            return self.ar.gemm_all_reduce(x, w, bits=self.bits, quant_type=self.quant_type)
         p = G.linear(x, w)
         return self.all_reduce(p, out=p)
 
@@ -278,29 +297,58 @@ class LlamaTP(nn.Module):
         return self.tp.gather_argmax(val, idx)
 
     @torch.no_grad()
+    def loss(self, ids: torch.Tensor) -> torch.Tensor:
+        """Mean next-token negative log-likelihood of ``ids [B, S]`` (perplexity = exp(loss)).
+
+        The lm_head is vocab-parallel, so the softmax statistics are combined across ranks
+        (max, sum of exponentials, target logit) with three small all-reduces.
+        """
+        B, S = ids.shape
+        x = self._hidden(ids, None)                              # [B*S, H], final norm applied
+        logits = G.linear(x, self.lm_head.weight).float()        # [B*S, V_local]
+        vs, vl = self.vocab_start, self.v_local
+        valid = min(vl, self.cfg.vocab_size - vs)
+        logits[:, valid:] = float("-inf")
+        tgt = ids[:, 1:].reshape(-1)
+        lg = logits.view(B, S, -1)[:, :-1].reshape(B * (S - 1), -1)
+        m = lg.max(dim=-1).values
+        if self.tp.world > 1:
+            dist.all_reduce(m, op=dist.ReduceOp.MAX, group=self.tp.group)
+        se = (lg - m[:, None]).exp().sum(-1)
+        local = (tgt >= vs) & (tgt < vs + valid)
+        t_logit = torch.where(local, lg.gather(1, (tgt - vs).clamp(0, vl - 1)[:, None]).squeeze(1),
+                              torch.zeros_like(m))
+        if self.tp.world > 1:
+            dist.all_reduce(se, group=self.tp.group)
+            dist.all_reduce(t_logit, group=self.tp.group)
+        return (se.log() + m - t_logit).mean()
+
+    def _hidden(self, ids: torch.Tensor, cache: Optional[KVCache]) -> torch.Tensor:
+        B, S = ids.shape
+        h = L.embedding(ids.reshape(-1), self.model.embed_tokens.weight)
+        pos = torch.arange(S, device=self.device, dtype=torch.int64).repeat(B)
+        slots = None
+        if cache is not None:
+            slots = cache.slots(torch.arange(B, device=self.device).repeat_interleave(S), pos)
+        x = L.rmsnorm(h, self.model.layers[0].input_layernorm.weight, self.cfg.rms_eps)
+
+        def attn(qkv, li):
+            return A.prefill_attention(qkv, B, S, self.nq, self.nkv, self.hd)
+
+        for li in range(self.cfg.num_layers):
+            x = self._layer(li, h, x, attn, pos, slots, cache)
+        if cache is not None:
+            cache.seq_lens.fill_(S)
+        return x
+
+    @torch.no_grad()
     def prefill(self, ids: torch.Tensor, cache: Optional[KVCache] = None, return_last_hidden: bool = False):
         """Causal forward over ``ids [B, S]`` (int64, on device); returns greedy next tokens [B].
 
         With ``cache``, k/v of all positions are written to it and ``seq_lens`` becomes S.
         """
         B, S = ids.shape
-        M = B * S
-        cfg = self.cfg
-        h = L.embedding(ids.reshape(-1), self.model.embed_tokens.weight)
-        pos = torch.arange(S, device=self.device, dtype=torch.int64).repeat(B)
-        slots = None
-        if cache is not None:
-            b_idx = torch.arange(B, device=self.device).repeat_interleave(S)
-            slots = cache.slots(b_idx, pos)
-        x = L.rmsnorm(h, self.model.layers[0].input_layernorm.weight, cfg.rms_eps)
-
-        def attn(qkv, li):
-            return A.prefill_attention(qkv, B, S, self.nq, self.nkv, self.hd)
-
-        for li in range(cfg.num_layers):
-            x = self._layer(li, h, x, attn, pos, slots, cache)
-        if cache is not None:
-            cache.seq_lens.fill_(S)
+        x = self._hidden(ids, cache)
         x_last = x.view(B, S, -1)[:, -1].contiguous()
         nxt = self._head(x_last)
         if return_last_hidden:

@@ -96,6 +96,30 @@ def test_ultimate_tp_mlp_single_rank(cuda_device):
     assert rel_l2(y.float(), ref.float()) < 0.02
 
 
+def test_loss_matches_hf_cross_entropy(cuda_device):
+    cfg = get_config("tiny")
+    m = LlamaTP(cfg, TPContext(device=cuda_device), cuda_device, init="full", seed=2)
+    hf32 = _hf(cfg, {k: v.float() for k, v in m.state_dict().items()}, cuda_device).float()
+    ids = torch.randint(0, cfg.vocab_size, (2, 50), device=cuda_device)
+    ours = float(m.loss(ids))
+    with torch.no_grad():
+        logits = hf32(ids).logits[:, :-1].reshape(-1, cfg.vocab_size)
+    ref = float(torch.nn.functional.cross_entropy(logits, ids[:, 1:].reshape(-1)))
+    assert abs(ours - ref) / ref < 0.02, (ours, ref)
+
+
+def test_reference_tables_and_qa_entry_points(cuda_device):
+    from quantized_flash_communication_b200.inference import run_qa_test
+    from quantized_flash_communication_b200.main import benchmark_all_tables
+    cfg = get_config("tiny")
+    m = LlamaTP(cfg, TPContext(device=cuda_device), cuda_device, init="shard", seed=1)
+    res = benchmark_all_tables(m, None, cuda_device, 0, block_list=(512, 128), volumes_mb=(1,), batches=(2,), seq=16)
+    assert len(res["table1"]) == cfg.num_layers and len(res["table2"]) == 2 and len(res["table4"]) == 1
+    assert all(r[1] > 0 for r in res["table1"])
+    toks, ms = run_qa_test(m, None, cuda_device, 0, max_new_tokens=4, verbose=False)
+    assert toks.shape == (1, 4) and ms > 0
+
+
 def test_cuda_graph_prefill_and_decode_match_eager(cuda_device):
     cfg = get_config("tiny")
     m = LlamaTP(cfg, TPContext(device=cuda_device), cuda_device, init="full", seed=4)
