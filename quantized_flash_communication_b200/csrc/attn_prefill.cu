@@ -2,8 +2,8 @@
 //
 // Replaces the attention of the reference's Hugging Face model (replicated on every rank,
 // main.py:194).  Inputs come straight from the fused qkv activation [B*S, (nq + 2 nkv) hd]
-// (after RoPE); V is first transposed into vt [B * nkv * hd, S_pad] so that both matrix
-// products read K-major operands with the same 128-byte-swizzled TMA layout as the GEMM.
+// (after RoPE).  Q and K tiles are K-major operands (head dim contiguous); V tiles, loaded
+// the same way, are the MN-major B operand of P V, so nothing is transposed.
 //
 // Persistent: one CTA per SM walks (128-query tile, query head, sequence) work items,
 // heaviest first; 10 warps:
@@ -37,7 +37,8 @@ constexpr int BQ = 128, BKV = 128;
 constexpr int TILE_BYTES = 128 * 128 * 2;  // one 128 x 128 bf16 operand (two 64-column swizzle tiles)
 constexpr int HALF_BYTES = TILE_BYTES / 2;
 constexpr int NUM_THREADS = 320;
-constexpr uint32_t IDESC = tc::idesc_f16(128, 128, true);
+constexpr uint32_t IDESC = tc::idesc_f16(128, 128, true);           // S = Q K^T, both K-major
+constexpr uint32_t IDESC_PV = tc::idesc_f16(128, 128, true, true);  // O = P V, V MN-major
 // smem: Q | K[2] | Vt[2] | P[2] | barriers + alpha/l
 constexpr int SMEM_BYTES = 7 * TILE_BYTES + 1024 + 2048;
 
@@ -80,8 +81,7 @@ QFC_DEV void item_coords(int i, const Args& a, int& qt, int& h, int& b) {
 // the same items, and a global tile counter t (over all items of this CTA) selects the
 // ring slot (t & 1) and mbarrier phase ((t >> 1) & 1) of every double buffer.
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmVT,
-                    const Args args) {
+attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
@@ -148,7 +148,6 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_cons
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       tc::tma_prefetch_desc(&tmQKV);
-      tc::tma_prefetch_desc(&tmVT);
       int t = 0, k = 0;
       int issued[2] = {-1, -1}, v_issued[2] = {-1, -1}, q_issued = -1;
       bool ok = true;
@@ -188,9 +187,9 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_cons
           }
           const uint32_t vb = tc::smem_u32(&v_full[st]);
           tc::mbar_arrive_expect_tx(vb, TILE_BYTES);
-          const int vrow = (b * args.nkv + kvh) * HD;
-          tc::tma_load_2d(tc::smem_u32(sV + st * TILE_BYTES), &tmVT, vb, j * BKV, vrow);
-          tc::tma_load_2d(tc::smem_u32(sV + st * TILE_BYTES + HALF_BYTES), &tmVT, vb, j * BKV + 64, vrow);
+          const int vcol = (args.nq + args.nkv + kvh) * HD;
+          tc::tma_load_2d(tc::smem_u32(sV + st * TILE_BYTES), &tmQKV, vb, vcol, row_base + j * BKV);
+          tc::tma_load_2d(tc::smem_u32(sV + st * TILE_BYTES + HALF_BYTES), &tmQKV, vb, vcol + 64, row_base + j * BKV);
           v_issued[st] = t;
         }
       }
@@ -251,12 +250,15 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_cons
           }
           tc::tc_fence_after();
           const uint32_t a0 = tc::smem_u32(sP + st * TILE_BYTES), b0 = tc::smem_u32(sV + st * TILE_BYTES);
+          // P: K-major, keys split in two 64-key swizzle tiles.  V: MN-major as loaded
+          // (rows = keys, 64 head dims per 128-byte row, second 64 dims HALF_BYTES later);
+          // 16 keys = 2048 bytes per MMA.
 #pragma unroll
           for (int s = 0; s < 2; ++s)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               tc::umma_f16(tmem + 256 + st * 128, tc::sw128_kmajor_desc(a0 + s * HALF_BYTES + kk * 32),
-                           tc::sw128_kmajor_desc(b0 + s * HALF_BYTES + kk * 32), IDESC, (s | kk) != 0);
+                           tc::sw128_mnmajor_desc(b0 + (s * 4 + kk) * 2048, HALF_BYTES), IDESC_PV, (s | kk) != 0);
           tc::umma_commit(tc::smem_u32(&o_full[st]));
           tc::umma_commit(tc::smem_u32(&p_empty[st]));
           tc::umma_commit(tc::smem_u32(&v_empty[st]));
@@ -290,14 +292,18 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_cons
         }
         tc::tc_fence_after();
         float sv[128];
+        {
+          uint32_t u[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t u[32];
-          tc::tmem_ld_32x32b_x32(tmem + st * 128 + lane_off + c * 32, u);
+          for (int c = 0; c < 4; ++c) tc::tmem_ld_32x32b_x32(tmem + st * 128 + lane_off + c * 32, u[c]);
+          tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[i]);
+          for (int c = 0; c < 4; ++c) {
+            tc::tmem_reg_fence(u[c]);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[c][i]);
+          }
         }
-        tc::tmem_wait_ld();
         tc::tc_fence_before();
         tc::mbar_arrive(tc::smem_u32(&s_empty[st]));
         // columns past kmax are masked: keys above the diagonal or past the sequence end
@@ -381,6 +387,7 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_cons
           uint32_t u[32];
           tc::tmem_ld_32x32b_x32(tmem + 256 + st * 128 + lane_off + c * 32, u);
           tc::tmem_wait_ld();
+          tc::tmem_reg_fence(u);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha, __uint_as_float(u[i]));
         }
@@ -408,25 +415,6 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_cons
   if (warp == 1) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
-  }
-}
-
-// vt[(b*nkv + kvh)*HD + d][s] = v[b*S + s][kvh*HD + d]  (32x32 tiles through shared memory)
-__global__ void transpose_v_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ vt, int B, int S,
-                                   int S_pad, int nq, int nkv) {
-  __shared__ __nv_bfloat16 tile[32][33];
-  const int ld = (nq + 2 * nkv) * HD;
-  const int bk = blockIdx.z;  // b * nkv + kvh
-  const int b = bk / nkv, kvh = bk % nkv;
-  const int s0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int s = s0 + i, d = d0 + threadIdx.x;
-    tile[i][threadIdx.x] = (s < S) ? qkv[(int64_t)(b * S + s) * ld + (nq + nkv + kvh) * HD + d] : __float2bfloat16(0.f);
-  }
-  __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int d = d0 + i, s = s0 + threadIdx.x;
-    if (s < S_pad) vt[((int64_t)bk * HD + d) * S_pad + s] = tile[threadIdx.x][i];
   }
 }
 
@@ -484,13 +472,6 @@ void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_
   if (B == 0 || S == 0) return;
   c10::cuda::CUDAGuard guard(qkv.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  const int64_t S_pad = (S + 7) / 8 * 8;
-  at::Tensor vt = at::empty({B * nkv * HD, S_pad}, qkv.options());
-  dim3 tgrid((unsigned)((S_pad + 31) / 32), HD / 32, (unsigned)(B * nkv));
-  transpose_v_kernel<<<tgrid, dim3(32, 8), 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
-                                                    reinterpret_cast<__nv_bfloat16*>(vt.data_ptr()), (int)B, (int)S,
-                                                    (int)S_pad, (int)nq, (int)nkv);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
   static bool attr_set[64] = {false};
   const int dev = qkv.get_device();
   if (!attr_set[dev]) {
@@ -498,7 +479,6 @@ void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_
     attr_set[dev] = true;
   }
   const CUtensorMap tq = make_map(qkv.data_ptr(), B * S, (nq + 2 * nkv) * HD, (nq + 2 * nkv) * HD);
-  const CUtensorMap tv = make_map(vt.data_ptr(), B * nkv * HD, S, S_pad);
   Args a;
   a.B = (int)B;
   a.S = (int)S;
@@ -514,7 +494,7 @@ void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t items = (int64_t)a.q_tiles * nq * B;
   const int grid = (int)std::min<int64_t>(items, sms);
-  attn_prefill_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tq, tv, a);
+  attn_prefill_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tq, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

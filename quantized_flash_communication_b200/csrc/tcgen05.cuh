@@ -143,11 +143,25 @@ QFC_DEV uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory descriptor for an MN-major tile written by TMA with 128-byte swizzling:
+// each 128-byte row holds 64 consecutive MN elements, 8 K-rows form a 1024-byte atom
+// (stride-dimension offset 1024), and the next 64-element block along MN starts
+// lbo_bytes later (leading-dimension offset).
+QFC_DEV uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16: fp32 accumulator, A/B bf16 (fmt 1) or fp16 (fmt 0),
-// both K-major, shape M x N.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16) {
-  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((uint32_t)(N >> 3) << 17) |
-         ((uint32_t)(M >> 4) << 24);
+// A K-major, B K-major (or MN-major with b_mn_major), shape M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool b_mn_major = false) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 }  // namespace tc
