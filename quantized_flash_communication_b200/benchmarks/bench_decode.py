@@ -1,0 +1,108 @@
+"""Prefill + decode benchmark (BASELINE configs 4 and 5).
+
+    torchrun --nproc-per-node N -m quantized_flash_communication_b200.benchmarks.bench_decode \
+        --model llama3-8b --batch 64 --ctx 4096 --new 128 --bits 8
+    torchrun --nproc-per-node 8 -m quantized_flash_communication_b200.benchmarks.bench_decode \
+        --model llama3-70b --batch 4 --ctx 2048 --new 128 --bits 4
+
+Random-init weights N(0, 0.02), uniformly random token ids.  The context is prefilled
+(timed: TTFT, CUDA events, max over ranks); then each decode step (one token for every
+sequence, one CUDA graph replay that includes the quantized all-reduces and the argmax
+combine) is timed over ``new - 1`` steps after ``--warmup`` untimed steps.  Rank 0 prints one
+JSON line: TTFT, per-token latency and decode tokens/s for the whole batch.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+import torch.distributed as dist
+
+from ..communication import reset_communicators
+from ..models.config import get_config
+from ..models.llama import LlamaTP, TPContext
+from ..utils.clocks import ClockSampler
+from ..utils.dist import init_distributed
+
+
+def _max(x: float, dev) -> float:
+    if not (dist.is_available() and dist.is_initialized()):
+        return x
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier():
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="llama3-8b")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--new", type=int, default=128)
+    ap.add_argument("--bits", type=int, default=8)
+    ap.add_argument("--group-size", type=int, default=128)
+    ap.add_argument("--ar-backend", default="qfc", choices=["qfc", "nccl"])
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (debug only)")
+    args = ap.parse_args(argv)
+    rank, world, dev = init_distributed()
+    cfg = get_config(args.model)
+    if args.layers:
+        cfg = cfg.with_layers(args.layers)
+    B, S = args.batch, args.ctx
+    tp = TPContext(None, dev, ar_backend=args.ar_backend, bits=args.bits, group_size=args.group_size,
+                   reserve_tokens=B * S, hidden_size=cfg.hidden_size)
+    model = LlamaTP(cfg, tp, dev, init="shard", seed=7)
+    cache = model.new_cache(B, S + args.new + args.warmup + 1)
+    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(1)).to(dev)
+    model.prefill(ids, cache)  # warm-up (JIT-free kernels; sizes the workspaces)
+    torch.cuda.synchronize()
+    _barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    tok = model.prefill(ids, cache)
+    e.record()
+    torch.cuda.synchronize()
+    ttft = _max(s.elapsed_time(e), dev)
+
+    step = model.capture_decode(cache)
+    cur = tok
+    for _ in range(args.warmup):
+        cur = step(cur).clone()
+    torch.cuda.synchronize()
+    _barrier()
+    n = max(1, args.new - 1)
+    sampler = ClockSampler(list(range(world)) if world > 1 else [dev.index]) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    s.record()
+    for _ in range(n):
+        cur = step(cur)
+    e.record()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.__exit__(None, None, None)
+    per_tok = _max(s.elapsed_time(e), dev) / n
+    if tp.ar is not None:
+        tp.ar.check()
+    step.release()
+    if rank == 0:
+        print(json.dumps({
+            "benchmark": "tp_decode", "model": cfg.name, "n_gpus": world, "batch": B, "ctx": S, "new_tokens": args.new,
+            "allreduce": f"{args.ar_backend} INT{args.bits} g{args.group_size}" if world > 1 else "none (tp1)",
+            "ttft_ms": ttft, "per_token_ms": per_tok, "decode_tokens_per_s": B * 1000.0 / per_tok,
+            "launch": "cuda_graph", "clocks": sampler.summary() if sampler else None,
+            "data": "synthetic: uniform random token ids, random-init N(0,0.02) weights"}), flush=True)
+    reset_communicators()
+    if dist.is_available() and dist.is_initialized():
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
