@@ -3,10 +3,12 @@
 // The reference decodes through Hugging Face's generate() and its KV cache
 // (inference.py:29); here the cache is paged per rank ([pages, kv_heads, page, head_dim])
 // and attention is split along the context ("flash-decoding"):
-//   pass 1: one CTA per (sequence, kv head, partition of kPart tokens); its 4 warps
-//           stream the partition's K and V rows (one 16-byte-per-lane coalesced row per
-//           warp step), every query head of the GQA group reuses each loaded row, and an
-//           online softmax keeps (max, sum, acc) per head; the CTA writes fp32 partials;
+//   pass 1: one CTA per (sequence, kv head, partition of 256..4096 tokens, chosen so the
+//           grid still fills the GPU); the partition's K and V rows stream through a
+//           shared-memory ring (cp.async).  GQA groups of 2..8 heads run both products on
+//           the tensor cores (mma.sync m16n8k16, K/V fragments by ldmatrix); multi-head
+//           attention splits each row over 4 lanes on the CUDA cores.  An online softmax
+//           keeps (max, sum, acc) per head; the CTA writes fp32 partials;
 //   pass 2: one warp per (sequence, query head) merges the partitions' partials.
 // The partials are scratch memory passed in by the caller.
 #include <ATen/ATen.h>
@@ -29,18 +31,12 @@ using namespace decode;
 template <typename T, int HD, int G>
 void launch_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& bt,
                    const at::Tensor& sl, at::Tensor& out, at::Tensor& part_o, at::Tensor& part_ml, int B, int nq,
-                   int nkv, int page, int n_parts, float scale, cudaStream_t st) {
-  dim3 grid(n_parts, nkv, B);
-  decode_partial_kernel<T, HD, G><<<grid, kWarps * 32, 0, st>>>(
+                   int nkv, int page_shift, int n_parts, int part_tok, float scale, cudaStream_t st) {
+  C10_CUDA_CHECK((decode_launch<T, HD, G>(
       reinterpret_cast<const T*>(q.data_ptr()), reinterpret_cast<const T*>(kc.data_ptr()),
-      reinterpret_cast<const T*>(vc.data_ptr()), bt.data_ptr<int>(), sl.data_ptr<int>(), part_o.data_ptr<float>(),
-      part_ml.data_ptr<float>(), nq, nkv, page, (int)bt.size(1), n_parts, scale);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-  const int warps = B * nq;
-  decode_combine_kernel<T, HD><<<(warps * 32 + 255) / 256, 256, 0, st>>>(
-      part_o.data_ptr<float>(), part_ml.data_ptr<float>(), sl.data_ptr<int>(), reinterpret_cast<T*>(out.data_ptr()),
-      nq, n_parts, warps);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+      reinterpret_cast<const T*>(vc.data_ptr()), bt.data_ptr<int>(), sl.data_ptr<int>(),
+      reinterpret_cast<T*>(out.data_ptr()), part_o.data_ptr<float>(), part_ml.data_ptr<float>(), B, nq, nkv,
+      page_shift, (int)bt.size(1), n_parts, part_tok, scale, st)));
 }
 
 }  // namespace
@@ -59,14 +55,17 @@ void attn_decode_cuda(const at::Tensor& q, const at::Tensor& kc, const at::Tenso
   c10::cuda::CUDAGuard guard(q.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int page = (int)kc.size(2);
+  const int page_shift = ilog2_exact(page);
+  TORCH_CHECK(page_shift >= 0, "attn_decode: page size must be a power of two");
   const int max_ctx = (int)bt.size(1) * page;
-  const int n_parts = (max_ctx + kPart - 1) / kPart;
+  const int part_tok = decode_part_tokens(B, (int)nkv, max_ctx, at::cuda::getCurrentDeviceProperties()->multiProcessorCount);
+  const int n_parts = (max_ctx + part_tok - 1) / part_tok;
   at::Tensor part_o = at::empty({(int64_t)B * nq * n_parts * hd}, q.options().dtype(at::kFloat));
   at::Tensor part_ml = at::empty({(int64_t)B * nq * n_parts * 2}, q.options().dtype(at::kFloat));
   const int G = (int)(nq / nkv);
   auto go = [&](auto tag) {
     using T = decltype(tag);
-#define QFC_DEC(HD_, G_) launch_decode<T, HD_, G_>(q, kc, vc, bt, sl, out, part_o, part_ml, B, (int)nq, (int)nkv, page, n_parts, (float)scale, st)
+#define QFC_DEC(HD_, G_) launch_decode<T, HD_, G_>(q, kc, vc, bt, sl, out, part_o, part_ml, B, (int)nq, (int)nkv, page_shift, n_parts, part_tok, (float)scale, st)
     if (hd == 128) {
       switch (G) {
         case 1: QFC_DEC(128, 1); break;

@@ -44,20 +44,33 @@ unsigned long long needed_bytes(int batch, int nq, int hd, int page, int max_pag
   return (unsigned long long)batch * nq * parts * (hd + 2) * sizeof(float);
 }
 
+int sm_count() {
+  static int sms[kMaxDevices] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  if (sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    sms[dev] = n;
+  }
+  return sms[dev];
+}
+
 template <typename T, int HD, int G>
 int launch(const void* q, const void* kc, const void* vc, const int* bt, const int* sl, void* out, int B, int nq,
            int nkv, int page, int max_pages, float scale, float* scratch, cudaStream_t st) {
-  const int n_parts = (max_pages * page + kPart - 1) / kPart;
+  const int page_shift = ilog2_exact(page);
+  if (page_shift < 0) return QFC_NOALLOC_ERR_BAD_ARGS;
+  const int max_ctx = max_pages * page;
+  const int part_tok = decode_part_tokens(B, nkv, max_ctx, sm_count());
+  const int n_parts = (max_ctx + part_tok - 1) / part_tok;
   float* part_o = scratch;
   float* part_ml = scratch + (size_t)B * nq * n_parts * HD;
-  dim3 grid(n_parts, nkv, B);
-  decode_partial_kernel<T, HD, G><<<grid, kWarps * 32, 0, st>>>(
-      static_cast<const T*>(q), static_cast<const T*>(kc), static_cast<const T*>(vc), bt, sl, part_o, part_ml, nq, nkv,
-      page, max_pages, n_parts, scale);
-  const int warps = B * nq;
-  decode_combine_kernel<T, HD><<<(warps * 32 + 255) / 256, 256, 0, st>>>(part_o, part_ml, sl, static_cast<T*>(out),
-                                                                           nq, n_parts, warps);
-  return cudaGetLastError() == cudaSuccess ? QFC_NOALLOC_OK : QFC_NOALLOC_ERR_CUDA;
+  const cudaError_t err = decode_launch<T, HD, G>(static_cast<const T*>(q), static_cast<const T*>(kc),
+                                                  static_cast<const T*>(vc), bt, sl, static_cast<T*>(out), part_o,
+                                                  part_ml, B, nq, nkv, page_shift, max_pages, n_parts, part_tok, scale,
+                                                  st);
+  return err == cudaSuccess ? QFC_NOALLOC_OK : QFC_NOALLOC_ERR_CUDA;
 }
 
 template <typename T>
@@ -119,7 +132,9 @@ const char* qfc_noalloc_error_string(int code) {
     case QFC_NOALLOC_ERR_TOO_LARGE:
       return "call needs more scratch than the 16 MiB compiled into the library "
              "(batch * q_heads * ceil(max_pages * page / 256) * (head_dim + 2) * 4 bytes)";
-    case QFC_NOALLOC_ERR_BAD_ARGS: return "bad arguments (null pointer, head_dim not 64/128, GQA group not 1/2/4/8, dtype)";
+    case QFC_NOALLOC_ERR_BAD_ARGS:
+      return "bad arguments (null pointer, head_dim not 64/128, GQA group not 1/2/4/8, page size not a power of two, "
+             "dtype)";
     case QFC_NOALLOC_ERR_CUDA: return "a CUDA runtime call failed";
     default: return "unknown error code";
   }

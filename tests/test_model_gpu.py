@@ -63,15 +63,25 @@ def test_prefill_and_decode_match_hf(cuda_device, name):
     assert int(cache.seq_lens[0]) == S + 1
 
 
-def test_decode_attention_vs_torch(cuda_device):
+@pytest.mark.parametrize("nq,nkv,hd,page,dtype", [
+    (16, 4, 128, 64, torch.bfloat16),
+    (8, 8, 128, 16, torch.bfloat16),
+    (8, 4, 128, 16, torch.float16),
+    (32, 4, 128, 32, torch.bfloat16),
+    (16, 16, 64, 16, torch.float16),
+    (8, 4, 64, 64, torch.bfloat16),
+    (16, 4, 64, 16, torch.bfloat16),
+    (16, 2, 64, 16, torch.float16),
+])
+def test_decode_attention_vs_torch(cuda_device, nq, nkv, hd, page, dtype):
     from quantized_flash_communication_b200.ops.attention import decode_attention
-    B, nq, nkv, hd, page = 5, 16, 4, 128, 64
+    B = 5
     lens = torch.tensor([1, 63, 64, 700, 1500], dtype=torch.int32, device=cuda_device)
-    pps = 24
-    kc = torch.randn(B * pps, nkv, page, hd, device=cuda_device, dtype=torch.bfloat16)
+    pps = (1500 + page - 1) // page + 1
+    kc = torch.randn(B * pps, nkv, page, hd, device=cuda_device, dtype=dtype)
     vc = torch.randn_like(kc)
     bt = torch.randperm(B * pps, device=cuda_device, dtype=torch.int32).view(B, pps).contiguous()
-    q = torch.randn(B, nq * hd, device=cuda_device, dtype=torch.bfloat16)
+    q = torch.randn(B, nq * hd, device=cuda_device, dtype=dtype) * 2
     o = decode_attention(q, kc, vc, bt, lens, nq, nkv, hd)
     for b in range(B):
         L = int(lens[b])
