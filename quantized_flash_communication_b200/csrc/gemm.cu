@@ -31,6 +31,7 @@
 
 #include <mutex>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -41,16 +42,27 @@ namespace qfc {
 namespace gemm {
 
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;        // 16 KiB
 constexpr int B_HALF_BYTES = 128 * BK * 2;  // 16 KiB
 constexpr int B_BYTES = 2 * B_HALF_BYTES;   // 32 KiB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 512;
 constexpr int GROUP_M = 16;
-constexpr uint32_t IDESC = tc::idesc_f16(BM, BN, true);
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+// Single CTA: a 128 x 256 tile per CTA, 4 stages of A + both B halves (48 KiB).
+// CTA pair (cta_group::2): a 256 x 256 tile per pair; each CTA loads its 128 rows of A and
+// one 128-row half of B per stage (32 KiB, 6 stages), the even CTA issues M=256 MMAs that
+// read both CTAs' shared memory, and each CTA's TMEM holds its 128 rows of the tile.  Per
+// FLOP a CTA loads a third less than alone.
+template <bool PAIR>
+struct Cfg {
+  static constexpr int STAGES = PAIR ? 6 : 4;
+  static constexpr int B_LOAD = PAIR ? B_HALF_BYTES : B_BYTES;  // B bytes this CTA loads per stage
+  static constexpr int STAGE_BYTES = A_BYTES + B_LOAD;
+  static constexpr int TILE_M = PAIR ? 2 * BM : BM;
+  static constexpr uint32_t IDESC = tc::idesc_f16(TILE_M, BN, true);
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
 
 // EPI_QS8 / EPI_QS4 / EPI_QS16: quantize each 128-column group of the (bf16-rounded) tile
 // to INT8 / INT4 / raw bf16 and store it into the owner rank's reduce-scatter slot.
@@ -150,15 +162,17 @@ QFC_DEV void fail(const GemmArgs& a, volatile int* s_abort, int code) {
 
 QFC_DEV uint32_t pack_bf16(float lo, float hi) { return pack_bf16x2(lo, hi); }
 
-template <int EPI>
+template <int EPI, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const GemmArgs args) {
+  using C = Cfg<PAIR>;
+  constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_LOAD);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
@@ -168,7 +182,11 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_tiles = (args.M + BM - 1) / BM;
+  // scheduling unit: a CTA, or a CTA pair (cluster of 2; rank 0 issues the MMAs)
+  const uint32_t crank = PAIR ? tc::cluster_ctarank() : 0u;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int m_tiles = (args.M + C::TILE_M - 1) / C::TILE_M;
   const int tiles = m_tiles * args.n_tiles;
   const int kbs = (args.K + BK - 1) / BK;
 
@@ -179,7 +197,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(tc::smem_u32(&tfull[b]), 1);
-      tc::mbar_init(tc::smem_u32(&tempty[b]), 128);
+      tc::mbar_init(tc::smem_u32(&tempty[b]), PAIR ? 256 : 128);  // epilogue threads (of both CTAs)
     }
     tc::mbar_init(tc::smem_u32(drain), 1);
     *s_abort = 0;
@@ -190,11 +208,17 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     tc::tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tc::tmem_alloc(tc::smem_u32(tmem_holder), TMEM_COLS);
-    tc::tmem_relinquish();
+    if constexpr (PAIR) {
+      tc::tmem_alloc_pair(tc::smem_u32(tmem_holder), TMEM_COLS);
+      tc::tmem_relinquish_pair();
+    } else {
+      tc::tmem_alloc(tc::smem_u32(tmem_holder), TMEM_COLS);
+      tc::tmem_relinquish();
+    }
   }
   tc::tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) tc::cluster_sync();  // the peer's barriers are initialised before any remote signal
+  else __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
@@ -205,7 +229,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int last_issue[STAGES];
       for (int s = 0; s < STAGES; ++s) last_issue[s] = -1;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      for (int tile = unit; tile < tiles && ok; tile += n_units) {
         int mb, nb;
         tile_coords(tile, m_tiles, args.n_tiles, mb, nb);
         const int yb = nb * args.b_first_step;
@@ -218,14 +242,23 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             break;
           }
           const uint32_t fb = tc::smem_u32(&full[s]);
-          tc::mbar_arrive_expect_tx(fb, STAGE_BYTES);
-          tc::tma_load_2d(tc::smem_u32(sA + s * A_BYTES), &tmA, fb, kb * BK, mb * BM);
-          tc::tma_load_2d(tc::smem_u32(sB + s * B_BYTES), &tmB, fb, kb * BK, yb);
-          tc::tma_load_2d(tc::smem_u32(sB + s * B_BYTES + B_HALF_BYTES), &tmB, fb, kb * BK, yb + args.b_second);
+          if constexpr (PAIR) {
+            // both CTAs' copies complete on the even CTA's barrier, which expects both
+            const uint32_t fb0 = tc::mapa_shared(fb, 0);
+            if (crank == 0) tc::mbar_arrive_expect_tx(fb, 2 * C::STAGE_BYTES);
+            tc::tma_load_2d_pair(tc::smem_u32(sA + s * A_BYTES), &tmA, fb0, kb * BK, mb * C::TILE_M + (int)crank * BM);
+            tc::tma_load_2d_pair(tc::smem_u32(sB + s * C::B_LOAD), &tmB, fb0, kb * BK,
+                                 crank ? yb + args.b_second : yb);
+          } else {
+            tc::mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+            tc::tma_load_2d(tc::smem_u32(sA + s * A_BYTES), &tmA, fb, kb * BK, mb * BM);
+            tc::tma_load_2d(tc::smem_u32(sB + s * C::B_LOAD), &tmB, fb, kb * BK, yb);
+            tc::tma_load_2d(tc::smem_u32(sB + s * C::B_LOAD + B_HALF_BYTES), &tmB, fb, kb * BK, yb + args.b_second);
+          }
           last_issue[s] = it;
         }
       }
-      if (!ok || *s_abort) {
+      if ((!ok || *s_abort) && crank == 0) {
         // Let every issued copy land before the CTA (and its shared memory) goes away.
         for (int s = 0; s < STAGES; ++s) {
           if (last_issue[s] < 0) continue;
@@ -237,11 +270,11 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && crank == 0) {
       int it = 0, t = 0;
       bool ok = true;
       bool issued = false;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++t) {
+      for (int tile = unit; tile < tiles && ok; tile += n_units, ++t) {
         const int buf = t & 1;
         if (!tc::mbar_wait(tc::smem_u32(&tempty[buf]), ((t >> 1) & 1) ^ 1, globaltimer_ns() + args.timeout_ns,
                            s_abort)) {
@@ -261,21 +294,28 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           }
           tc::tc_fence_after();
           const uint32_t a0 = tc::smem_u32(sA + s * A_BYTES);
-          const uint32_t b0 = tc::smem_u32(sB + s * B_BYTES);
+          const uint32_t b0 = tc::smem_u32(sB + s * C::B_LOAD);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            tc::umma_f16(tmem_d, tc::sw128_kmajor_desc(a0 + k * 32), tc::sw128_kmajor_desc(b0 + k * 32), IDESC,
-                         (kb | k) != 0);
+            if constexpr (PAIR)
+              tc::umma_f16_pair(tmem_d, tc::sw128_kmajor_desc(a0 + k * 32), tc::sw128_kmajor_desc(b0 + k * 32),
+                                C::IDESC, (kb | k) != 0);
+            else
+              tc::umma_f16(tmem_d, tc::sw128_kmajor_desc(a0 + k * 32), tc::sw128_kmajor_desc(b0 + k * 32), C::IDESC,
+                           (kb | k) != 0);
           }
           issued = true;
-          tc::umma_commit(tc::smem_u32(&empty[s]));
+          if constexpr (PAIR) tc::umma_commit_pair(tc::smem_u32(&empty[s]), 0x3);
+          else tc::umma_commit(tc::smem_u32(&empty[s]));
         }
         if (!ok) break;
-        tc::umma_commit(tc::smem_u32(&tfull[buf]));
+        if constexpr (PAIR) tc::umma_commit_pair(tc::smem_u32(&tfull[buf]), 0x3);
+        else tc::umma_commit(tc::smem_u32(&tfull[buf]));
       }
       if ((!ok || *s_abort) && issued) {
         // Wait for the MMAs already issued before TMEM is released.
-        tc::umma_commit(tc::smem_u32(drain));
+        if constexpr (PAIR) tc::umma_commit_pair(tc::smem_u32(drain), 0x1);
+        else tc::umma_commit(tc::smem_u32(drain));
         int never = 0;
         tc::mbar_wait(tc::smem_u32(drain), 0, globaltimer_ns() + 50000000ull, &never);
       }
@@ -285,7 +325,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const int q = warp & 3;  // the TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
     int t = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+    for (int tile = unit; tile < tiles; tile += n_units, ++t) {
       int mb, nb;
       tile_coords(tile, m_tiles, args.n_tiles, mb, nb);
       const int buf = t & 1;
@@ -295,7 +335,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
       tc::tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
-      const int row = mb * BM + row_in_tile;
+      const int row = mb * C::TILE_M + (int)crank * BM + row_in_tile;
       const int col0 = nb * args.n_tile_cols;
       if constexpr (is_qs(EPI)) {
         constexpr int P = EPI == EPI_QS8 ? 8 : (EPI == EPI_QS4 ? 4 : 16);
@@ -398,7 +438,8 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
       }
       tc::tc_fence_before();
-      tc::mbar_arrive(tc::smem_u32(&tempty[buf]));
+      if constexpr (PAIR) tc::mbar_arrive_cluster(tc::mapa_shared(tc::smem_u32(&tempty[buf]), 0));
+      else tc::mbar_arrive(tc::smem_u32(&tempty[buf]));
     }
     // Peer stores of this thread are visible system-wide before the CTA reports done.
     if constexpr (is_qs(EPI)) __threadfence_system();
@@ -423,9 +464,12 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
     }
   }
+  // No CTA of a pair leaves (or frees TMEM) while its peer may still signal its barriers.
+  if constexpr (PAIR) tc::cluster_sync();
   if (warp == 1) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR) tc::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tc::tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -474,22 +518,55 @@ int* status_word() {
   return p;
 }
 
+// CTA-pair GEMMs are on unless QFC_GEMM_PAIR=0 (kept for A/B measurements).
+bool pair_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("QFC_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 int sm_count(int dev) {
   static int cached[64] = {0};
   if (cached[dev] == 0) cudaDeviceGetAttribute(&cached[dev], cudaDevAttrMultiProcessorCount, dev);
   return cached[dev];
 }
 
+template <int EPI, bool PAIR>
+void launch_cfg(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& a, int M, int dev, int max_ctas) {
+  using C = Cfg<PAIR>;
+  static bool attr_set[64] = {false};
+  auto kern = gemm_bf16_kernel<EPI, PAIR>;
+  if (!attr_set[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  const int tiles = ((M + C::TILE_M - 1) / C::TILE_M) * a.n_tiles;
+  const int per_unit = PAIR ? 2 : 1;
+  int units = std::min(tiles, sm_count(dev) / per_unit);
+  if (max_ctas > 0) units = std::min(units, std::max(1, max_ctas / per_unit));
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(units * per_unit);
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = per_unit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = PAIR ? 1 : 0;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tA, tB, a));
+}
+
+// CTA pairs serve M >= 256 (a 256-row tile per pair); smaller M runs one CTA per tile.
 template <int EPI>
 void launch(const at::Tensor& A, const at::Tensor& B, at::Tensor* D, const at::Tensor* R, int M, int N, int K,
             double timeout_ms, int max_ctas, const ScatterArgs* sc = nullptr) {
-  static bool attr_set[64] = {false};
   const int dev = A.get_device();
-  auto kern = gemm_bf16_kernel<EPI>;
-  if (!attr_set[dev]) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr_set[dev] = true;
-  }
   GemmArgs a;
   a.M = M;
   a.N = N;
@@ -514,11 +591,9 @@ void launch(const at::Tensor& A, const at::Tensor& B, at::Tensor* D, const at::T
   a.timeout_ns = (uint64_t)(timeout_ms * 1e6);
   const CUtensorMap tA = make_tmap(A.data_ptr(), M, K, A.stride(0), BM);
   const CUtensorMap tB = make_tmap(B.data_ptr(), B.size(0), K, B.stride(0), 128);
-  const int tiles = ((M + BM - 1) / BM) * a.n_tiles;
-  int grid = std::min(tiles, sm_count(dev));
-  if (max_ctas > 0) grid = std::min(grid, max_ctas);
-  kern<<<grid, NUM_THREADS, SMEM_BYTES, at::cuda::getCurrentCUDAStream()>>>(tA, tB, a);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const bool pair = M >= 2 * BM && pair_enabled() && (max_ctas <= 0 || max_ctas >= 2);
+  if (pair) launch_cfg<EPI, true>(tA, tB, a, M, dev, max_ctas);
+  else launch_cfg<EPI, false>(tA, tB, a, M, dev, max_ctas);
 }
 
 void check_operand(const at::Tensor& t, const char* name) {

@@ -1,7 +1,7 @@
 // Thin inline-PTX wrappers for the Blackwell (sm_100a) tensor-core path: mbarriers, TMA
-// tile loads (never with .multicast::cluster: these kernels run on multi-GPU jobs whose
-// operands may be peer memory), tcgen05 MMA / commit / TMEM alloc / TMEM loads, and the
-// shared-memory and instruction descriptors.  Written from the PTX ISA's descriptions of
+// tile loads (plain loads only, never multicast: these kernels run in multi-GPU jobs
+// whose operands may be peer memory), CTA-pair helpers, tcgen05 MMA / commit / TMEM
+// alloc / TMEM loads, and the shared-memory and instruction descriptors.  Written from the PTX ISA's descriptions of
 // these instructions.
 #pragma once
 
@@ -78,6 +78,37 @@ QFC_DEV void tma_prefetch_desc(const CUtensorMap* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
+// ---------------------------------------------------------------- clusters (CTA pairs)
+QFC_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster.
+QFC_DEV uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+// Every thread of every CTA of the cluster; release / acquire at cluster scope.
+QFC_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier anywhere in the cluster (shared::cluster address).
+QFC_DEV void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// TMA tile load into this CTA's shared memory whose completion is signalled on an mbarrier
+// of either CTA of the pair (cluster_bar is a shared::cluster address).  Plain load: no
+// multicast.
+QFC_DEV void tma_load_2d_pair(uint32_t smem_dst, const CUtensorMap* tmap, uint32_t cluster_bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(cluster_bar), "r"(x), "r"(y)
+      : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 QFC_DEV void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
@@ -104,6 +135,38 @@ QFC_DEV void umma_f16(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_
 // Arrive on an mbarrier once every previously issued tcgen05.mma of this thread is done.
 QFC_DEV void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// CTA-pair forms (cta_group::2): TMEM is allocated / freed by one warp of each CTA of the
+// pair together; the MMA is issued by the even CTA and spans both CTAs' shared memory
+// (A rows and B rows split between them at the same offsets) and both CTAs' TMEM.
+QFC_DEV void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+QFC_DEV void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+QFC_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+QFC_DEV void umma_f16_pair(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n"
+      "}\n" ::"r"(tmem_d),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the mbarrier at offset `bar` of every CTA in cta_mask when the pair's
+// previously issued MMAs are done (commit with a CTA mask; not a data load).
+QFC_DEV void umma_commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   bar),
+               "h"(cta_mask)
+               : "memory");
 }
 
 // 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives lane

@@ -16,7 +16,9 @@ from conftest import free_port
 
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
-WORLD = min(torch.cuda.device_count(), 4) if torch.cuda.is_available() else 0
+# QFC_TEST_WORLD raises the rank count (default: up to 4 of the visible GPUs).
+WORLD = (min(torch.cuda.device_count(), int(os.environ.get("QFC_TEST_WORLD", "4")))
+         if torch.cuda.is_available() else 0)
 need2 = pytest.mark.skipif(WORLD < 2, reason="needs >= 2 GPUs")
 
 
