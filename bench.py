@@ -44,6 +44,8 @@ def _parse():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch kernels eagerly instead of one CUDA graph")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="print per-operator device times of eager steps instead of the benchmark line")
     ap.add_argument("--no-fuse-gemm", action="store_true",
                     help="run o_proj/down_proj GEMMs and the all-reduce as separate kernels")
     return ap.parse_args()
@@ -130,6 +132,37 @@ def _timed_e2e(step_fn, args, dev):
 
 
 # ------------------------------------------------------------------------------------------
+def _breakdown(args, model, tp, ids, cache, dev, rank, world):
+    """Eager steps with per-operator CUDA-event regions; prints max-over-ranks totals."""
+    import torch
+    import torch.distributed as dist
+    from quantized_flash_communication_b200.utils.trace import OpTimer
+
+    for _ in range(args.warmup):
+        model.prefill(ids, cache)
+    timer = OpTimer()
+    model.timer = tp.timer = timer
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        model.prefill(ids, cache)
+    e.record()
+    summ = timer.summary()
+    model.timer = tp.timer = None
+    names = list(summ.keys())
+    vals = torch.tensor([summ[n]["ms"] / args.steps for n in names] + [s.elapsed_time(e) / args.steps],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        out = {n: round(float(v), 4) for n, v in zip(names, vals[:-1].tolist())}
+        print(json.dumps({"breakdown_ms_per_step_max_over_ranks": out, "eager_ms_per_step": float(vals[-1]),
+                          "n_gpus": world, "fuse_gemm": not args.no_fuse_gemm, "ar_backend": args.ar_backend,
+                          "counts_per_step": {n: summ[n]["count"] // args.steps for n in names}}), flush=True)
+    return None
+
+
 def run_ours(args):
     import torch
     sys.path.insert(0, ROOT)
@@ -154,6 +187,9 @@ def run_ours(args):
         model.prefill(ids, cache)
     torch.cuda.synchronize()
     launches_per_step = cnt["kernels"]
+    if args.breakdown:
+        _breakdown(args, model, tp, ids, cache, dev, rank, world)
+        return rank, None
     graphed = None
     if not args.no_graph:
         graphed = model.capture_prefill(B, S, cache)
@@ -207,7 +243,8 @@ def run_ours(args):
         "data": "synthetic: uniform random token ids, random-init N(0,0.02) weights",
         "config": {"model": cfg.name, "global_batch": B, "seq_len": S, "parallelism": f"tp{world}",
                    "allreduce": (f"qfc INT{args.bits} g{args.group_size} {args.quant_type}"
-                                 + (", scatter fused into o/down GEMM epilogues" if tp.fuse_gemm else "")
+                                 + (", scatter fused into o/down GEMM epilogues"
+                                    if tp.fuse_gemm and world <= tp.fuse_max_world else "")
                                  if args.ar_backend == "qfc" else args.ar_backend) if world > 1 else "none (tp1)",
                    "attention": A.prefill_backend(),
                    "launch": "cuda_graph" if graphed is not None else "eager",
@@ -301,7 +338,7 @@ def main():
         rank, res = run_reference(args) if args.impl == "reference" else run_ours(args)
     except SystemExit:
         raise
-    if rank == 0:
+    if rank == 0 and res is not None:
         print(json.dumps(res), flush=True)
     try:
         import torch.distributed as dist

@@ -78,37 +78,55 @@ rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ residual, T* __res
 // Rotary embedding (rotate-half convention) applied in place to q and k of the fused
 // qkv activation [M, (nq + 2*nkv) * hd], and k / v copied into the paged cache
 // k_cache / v_cache [num_pages, nkv, page, hd] at slot_mapping[m] (page * page_size +
-// offset; negative = do not cache).  One warp per (token, head); hd = 64 or 128.
-template <typename T>
+// offset; negative = do not cache).  One thread per (token, head, 8-element slice j of
+// the first half): it loads the 16-byte slices j of both halves, rotates them with the
+// (cos, sin) pairs of positions j*8 .. j*8+7 and stores both back (q, k) and into the
+// cache (k, v).  Every access is a 16-byte vector; hd = 64 or 128.
+template <typename T, int HD>
 __global__ void rope_kv_kernel(T* __restrict__ qkv, const int64_t* __restrict__ pos, const float2* __restrict__ cs,
                                T* __restrict__ k_cache, T* __restrict__ v_cache,
-                               const int64_t* __restrict__ slot_mapping, int64_t M, int nq, int nkv, int hd,
-                               int page) {
-  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const int heads = nq + 2 * nkv;
-  if (gw >= M * heads) return;
-  const int64_t m = gw / heads;
-  const int h = (int)(gw % heads);
-  T* row = qkv + m * (int64_t)heads * hd + (int64_t)h * hd;
-  const int half = hd >> 1;
-  if (h < nq + nkv) {
-    const float2* c = cs + pos[m] * half;
-    for (int i = lane; i < half; i += 32) {
-      const float2 a = c[i];  // (cos, sin)
-      const float x1 = to_f32(row[i]), x2 = to_f32(row[i + half]);
-      row[i] = from_f32<T>(x1 * a.x - x2 * a.y);
-      row[i + half] = from_f32<T>(x2 * a.x + x1 * a.y);
+                               const int64_t* __restrict__ slot_mapping, int64_t M, int nq, int nkv, int page,
+                               int page_shift) {
+  constexpr int HALF = HD / 2, HJ = HALF / 8;
+  const uint32_t heads = (uint32_t)(nq + 2 * nkv);
+  const int64_t total = M * heads * HJ;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(t % HJ);
+    const uint64_t hh = (uint64_t)(t / HJ);
+    const uint32_t h = (uint32_t)(hh % heads);
+    const int64_t m = (int64_t)(hh / heads);
+    T* row = qkv + (m * heads + h) * HD;
+    float x1[8], x2[8];
+    Vec8IO<T>::load(row + j * 8, x1);
+    Vec8IO<T>::load(row + HALF + j * 8, x2);
+    if (h < (uint32_t)(nq + nkv)) {
+      const float4* c = reinterpret_cast<const float4*>(cs + pos[m] * HALF + j * 8);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 a = c[i];  // (cos, sin) of elements 2i and 2i+1
+        float y1 = x1[2 * i] * a.x - x2[2 * i] * a.y, y2 = x2[2 * i] * a.x + x1[2 * i] * a.y;
+        x1[2 * i] = y1;
+        x2[2 * i] = y2;
+        y1 = x1[2 * i + 1] * a.z - x2[2 * i + 1] * a.w;
+        y2 = x2[2 * i + 1] * a.z + x1[2 * i + 1] * a.w;
+        x1[2 * i + 1] = y1;
+        x2[2 * i + 1] = y2;
+      }
+      Vec8IO<T>::store(row + j * 8, x1);
+      Vec8IO<T>::store(row + HALF + j * 8, x2);
     }
-  }
-  if (h >= nq && slot_mapping != nullptr) {
-    const int64_t slot = slot_mapping[m];
-    if (slot >= 0) {
-      __syncwarp();
-      const int64_t pg = slot / page, off = slot % page;
-      const int kvh = (h < nq + nkv) ? h - nq : h - nq - nkv;
-      T* dst = (h < nq + nkv ? k_cache : v_cache) + ((pg * nkv + kvh) * (int64_t)page + off) * hd;
-      for (int i = lane; i < hd; i += 32) dst[i] = row[i];
+    if (h >= (uint32_t)nq && slot_mapping != nullptr) {
+      const int64_t slot = slot_mapping[m];
+      if (slot >= 0) {
+        const int64_t pg = page_shift >= 0 ? slot >> page_shift : slot / page;
+        const int64_t off = page_shift >= 0 ? slot & (page - 1) : slot % page;
+        const bool is_k = h < (uint32_t)(nq + nkv);
+        const int kvh = is_k ? (int)h - nq : (int)h - nq - nkv;
+        T* dst = (is_k ? k_cache : v_cache) + ((pg * nkv + kvh) * (int64_t)page + off) * HD;
+        // the stored k is the bf16/fp16 value written back to qkv above
+        Vec8IO<T>::store(dst + j * 8, x1);
+        Vec8IO<T>::store(dst + HALF + j * 8, x2);
+      }
     }
   }
 }
@@ -265,16 +283,25 @@ void rope_kv_cuda(at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& cos_
     TORCH_CHECK(k_cache->dim() == 4, "rope_kv: cache must be [pages, nkv, page, hd]");
     page = (int)k_cache->size(2);
   }
-  const int64_t warps = M * (nq + 2 * nkv);
+  TORCH_CHECK(hd == 64 || hd == 128, "rope_kv: head_dim must be 64 or 128");
+  int page_shift = -1;
+  for (int sh = 0; sh < 31; ++sh)
+    if ((1 << sh) == page) page_shift = sh;
+  const int64_t total = M * (nq + 2 * nkv) * (hd / 16);
   const int threads = 256;
-  const int64_t blocks = (warps * 32 + threads - 1) / threads;
+  const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 8);
   QFC_DISPATCH_16(qkv.scalar_type(), [&] {
-    rope_kv_kernel<scalar_t><<<blocks, threads, 0, st>>>(
-        reinterpret_cast<scalar_t*>(qkv.data_ptr()), pos.data_ptr<int64_t>(),
-        reinterpret_cast<const float2*>(cos_sin.data_ptr()),
-        cache ? reinterpret_cast<scalar_t*>(k_cache->data_ptr()) : nullptr,
-        cache ? reinterpret_cast<scalar_t*>(v_cache->data_ptr()) : nullptr,
-        cache ? slot_mapping->data_ptr<int64_t>() : nullptr, M, (int)nq, (int)nkv, (int)hd, page);
+    auto* q = reinterpret_cast<scalar_t*>(qkv.data_ptr());
+    auto* csp = reinterpret_cast<const float2*>(cos_sin.data_ptr());
+    auto* kcp = cache ? reinterpret_cast<scalar_t*>(k_cache->data_ptr()) : nullptr;
+    auto* vcp = cache ? reinterpret_cast<scalar_t*>(v_cache->data_ptr()) : nullptr;
+    const int64_t* sm = cache ? slot_mapping->data_ptr<int64_t>() : nullptr;
+    if (hd == 128)
+      rope_kv_kernel<scalar_t, 128><<<blocks, threads, 0, st>>>(q, pos.data_ptr<int64_t>(), csp, kcp, vcp, sm, M,
+                                                                 (int)nq, (int)nkv, page, page_shift);
+    else
+      rope_kv_kernel<scalar_t, 64><<<blocks, threads, 0, st>>>(q, pos.data_ptr<int64_t>(), csp, kcp, vcp, sm, M,
+                                                                (int)nq, (int)nkv, page, page_shift);
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

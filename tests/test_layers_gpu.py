@@ -36,8 +36,9 @@ def _rope_ref(x, pos, cs):
     return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
 
 
-def test_rope_and_cache(cuda_device):
-    nq, nkv, hd, M, page = 8, 2, 128, 50, 16
+@pytest.mark.parametrize("hd,page", [(128, 16), (64, 16), (128, 24)])
+def test_rope_and_cache(cuda_device, hd, page):
+    nq, nkv, M = 8, 2, 50
     cs = L.rope_cos_sin(4096, hd, 10000.0, cuda_device)
     qkv = torch.randn(M, (nq + 2 * nkv) * hd, device=cuda_device, dtype=torch.bfloat16)
     pos = torch.randint(0, 4096, (M,), device=cuda_device)
@@ -45,6 +46,7 @@ def test_rope_and_cache(cuda_device):
     kc = torch.zeros(8, nkv, page, hd, device=cuda_device, dtype=torch.bfloat16)
     vc = torch.zeros_like(kc)
     slots = torch.randperm(8 * page, device=cuda_device)[:M]
+    slots[::7] = -1  # not cached
     L.rope_kv(qkv, pos, cs, nq, nkv, hd, kc, vc, slots)
     out = qkv.view(M, nq + 2 * nkv, hd)
     ref_q = _rope_ref(orig[:, :nq], pos, cs)
@@ -52,9 +54,12 @@ def test_rope_and_cache(cuda_device):
     assert torch.allclose(out[:, :nq].float(), ref_q, atol=2e-2, rtol=2e-2)
     assert torch.allclose(out[:, nq:nq + nkv].float(), ref_k, atol=2e-2, rtol=2e-2)
     assert torch.equal(out[:, nq + nkv:], orig[:, nq + nkv:])
-    pg, off = slots // page, slots % page
-    assert torch.equal(kc[pg, :, off], out[:, nq:nq + nkv])
-    assert torch.equal(vc[pg, :, off], out[:, nq + nkv:])
+    keep = slots >= 0
+    pg, off = slots[keep] // page, slots[keep] % page
+    assert torch.equal(kc[pg, :, off], out[keep, nq:nq + nkv])
+    assert torch.equal(vc[pg, :, off], out[keep, nq + nkv:])
+    written = (kc.abs().sum(-1) > 0).sum().item()
+    assert written == int(keep.sum()) * nkv
 
 
 def test_silu_mul(cuda_device):
