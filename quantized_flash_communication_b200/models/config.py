@@ -26,6 +26,28 @@ class LlamaConfig:
     def with_layers(self, n: int) -> "LlamaConfig":
         return replace(self, num_layers=n)
 
+    @classmethod
+    def from_hf_dict(cls, d: dict, name: str = "hf") -> "LlamaConfig":
+        """From a Hugging Face Llama ``config.json`` (or ``LlamaConfig.to_dict()``)."""
+        heads = d["num_attention_heads"]
+        return cls(name=name, hidden_size=d["hidden_size"], intermediate_size=d["intermediate_size"],
+                   num_layers=d["num_hidden_layers"], num_heads=heads,
+                   num_kv_heads=d.get("num_key_value_heads") or heads, vocab_size=d["vocab_size"],
+                   head_dim=d.get("head_dim") or d["hidden_size"] // heads, rms_eps=d.get("rms_norm_eps", 1e-5),
+                   rope_theta=d.get("rope_theta", 10000.0), rope_scaling=d.get("rope_scaling"),
+                   max_position=d.get("max_position_embeddings", 8192),
+                   tie_word_embeddings=bool(d.get("tie_word_embeddings", False)))
+
+    def to_hf_dict(self) -> dict:
+        """A Hugging Face ``LlamaForCausalLM`` config.json for this architecture."""
+        return {"architectures": ["LlamaForCausalLM"], "model_type": "llama", "hidden_size": self.hidden_size,
+                "intermediate_size": self.intermediate_size, "num_hidden_layers": self.num_layers,
+                "num_attention_heads": self.num_heads, "num_key_value_heads": self.num_kv_heads,
+                "vocab_size": self.vocab_size, "head_dim": self.head_dim, "rms_norm_eps": self.rms_eps,
+                "rope_theta": self.rope_theta, "rope_scaling": self.rope_scaling,
+                "max_position_embeddings": self.max_position, "tie_word_embeddings": self.tie_word_embeddings,
+                "hidden_act": "silu", "torch_dtype": "bfloat16"}
+
 
 PRESETS = {
     # BASELINE config 3: Llama-2-7B (MHA, SwiGLU 11008, vocab 32000)

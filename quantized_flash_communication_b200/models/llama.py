@@ -217,6 +217,9 @@ class LlamaTP(nn.Module):
 
     def __init__(self, cfg: LlamaConfig | str, tp: Optional[TPContext] = None, device=None,
                  dtype: torch.dtype = torch.bfloat16, init: str = "shard", seed: int = 0, init_std: float = 0.02):
+        """``init``: "shard" (random N(0, init_std) per rank), "full" (random full tensors
+        from ``seed``, then this rank's slice: every TP degree gets the same model) or
+        "empty" (uninitialised, for ``load_hf_state_dict`` / ``from_pretrained``)."""
         super().__init__()
         cfg = get_config(cfg) if isinstance(cfg, str) else cfg
         self.cfg = cfg
@@ -235,6 +238,8 @@ class LlamaTP(nn.Module):
         self.vocab_start = r * self.v_local
 
         def rnd(shape, full_shape=None, slicer=None, key=0):
+            if init == "empty":  # weights come from a checkpoint (load_hf_state_dict)
+                return torch.empty(shape, device=device, dtype=dtype)
             if init == "full":
                 g = torch.Generator(device=device).manual_seed(seed * 1000003 + key)
                 t = torch.empty(full_shape, device=device, dtype=dtype).normal_(0.0, init_std, generator=g)
@@ -271,6 +276,118 @@ class LlamaTP(nn.Module):
         self.timer = None  # utils.trace.OpTimer: per-operator device times of eager steps
 
     # --------------------------------------------------------------------------------------
+    # ------------------------------------------------------------------ checkpoints
+    # The reference loads Hugging Face weights with from_pretrained and slices the MLP in
+    # memory (main.py:25-39, 190-194).  Here every decoder weight is sharded: rows of
+    # q/k/v/gate/up (by head / by intermediate unit), columns of o_proj/down_proj, rows of
+    # the vocab-parallel lm_head (padded to a multiple of the TP degree); the embedding and
+    # the norms are replicated.
+    def _split_dim(self, name: str) -> Optional[int]:
+        if name == "lm_head.weight" or any(t in name for t in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj")):
+            return 0
+        if "o_proj" in name or "down_proj" in name:
+            return 1
+        return None
+
+    def _shard_of(self, name: str, full) -> torch.Tensor:
+        """This rank's part of the full tensor ``full`` (a tensor or a safetensors slice)."""
+        W, r = self.tp.world, self.tp.rank
+        dim = self._split_dim(name)
+        if dim is None or W == 1 and name != "lm_head.weight":
+            return full[:] if not isinstance(full, torch.Tensor) else full
+        if name == "lm_head.weight":
+            lo = self.vocab_start
+            hi = min(lo + self.v_local, self.cfg.vocab_size)
+            part = full[lo:hi] if hi > lo else None
+            out = torch.zeros(self.v_local, self.cfg.hidden_size, dtype=self.dtype)
+            if part is not None:
+                out[: hi - lo] = part.to(self.dtype)
+            return out
+        n = (full.shape[dim] if isinstance(full, torch.Tensor) else full.get_shape()[dim]) // W
+        return full[r * n:(r + 1) * n] if dim == 0 else full[:, r * n:(r + 1) * n]
+
+    @torch.no_grad()
+    def load_hf_state_dict(self, sd, strict: bool = True) -> None:
+        """Copy this rank's shard out of a full (unsharded) Hugging Face Llama state dict.
+
+        ``sd`` maps HF names to full tensors (or lazily sliceable safetensors entries).  With
+        ``tie_word_embeddings`` a missing ``lm_head.weight`` is taken from the embedding.
+        """
+        own = dict(self.named_parameters())
+        missing = []
+        for name, p in own.items():
+            src_name = name
+            if name not in sd and name == "lm_head.weight" and "model.embed_tokens.weight" in sd:
+                src_name = "model.embed_tokens.weight"
+            if src_name not in sd:
+                missing.append(name)
+                continue
+            part = self._shard_of(name, sd[src_name])
+            if tuple(part.shape) != tuple(p.shape):
+                raise ValueError(f"{name}: checkpoint shard {tuple(part.shape)} != parameter {tuple(p.shape)}")
+            p.data.copy_(part.to(device=p.device, dtype=p.dtype))
+        if strict and missing:
+            raise KeyError(f"checkpoint lacks {missing[:4]}{' ...' if len(missing) > 4 else ''}")
+
+    @torch.no_grad()
+    def full_state_dict(self) -> "dict[str, torch.Tensor]":
+        """The unsharded Hugging Face state dict, gathered from every rank (on every rank,
+        on the CPU).  Collective: all ranks of the group must call it."""
+        W = self.tp.world
+        out = {}
+        for name, p in self.named_parameters():
+            dim = self._split_dim(name)
+            t = p.detach()
+            if W > 1 and dim is not None:
+                parts = [torch.empty_like(t) for _ in range(W)]
+                dist.all_gather(parts, t.contiguous(), group=self.tp.group)
+                t = torch.cat(parts, dim)
+            if name == "lm_head.weight":
+                t = t[: self.cfg.vocab_size]
+            out[name] = t.cpu().clone()
+        return out
+
+    def save_pretrained(self, path: str) -> None:
+        """Write a Hugging Face style checkpoint (config.json + model.safetensors) of the full
+        model from rank 0.  Collective (gathers the shards)."""
+        import json
+        import os
+        from safetensors.torch import save_file
+        full = self.full_state_dict()
+        if self.tp.rank == 0:
+            os.makedirs(path, exist_ok=True)
+            if self.cfg.tie_word_embeddings:
+                full.pop("lm_head.weight", None)
+            save_file({k: v.contiguous() for k, v in full.items()}, os.path.join(path, "model.safetensors"))
+            with open(os.path.join(path, "config.json"), "w") as f:
+                json.dump(self.cfg.to_hf_dict(), f, indent=1)
+        if self.tp.world > 1:
+            dist.barrier(group=self.tp.group)
+
+    @classmethod
+    def from_pretrained(cls, path: str, tp: Optional[TPContext] = None, device=None,
+                        dtype: torch.dtype = torch.bfloat16) -> "LlamaTP":
+        """Build this rank's shard from a Hugging Face Llama checkpoint directory
+        (config.json + *.safetensors).  Each rank reads only its slices of the files."""
+        import glob
+        import json
+        import os
+        from safetensors import safe_open
+        with open(os.path.join(path, "config.json")) as f:
+            cfg = LlamaConfig.from_hf_dict(json.load(f), name=os.path.basename(os.path.normpath(path)))
+        model = cls(cfg, tp, device, dtype=dtype, init="empty")
+        files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
+        if not files:
+            raise FileNotFoundError(f"no *.safetensors under {path}")
+        handles = [safe_open(fn, framework="pt", device="cpu") for fn in files]
+        index = {}
+        for h in handles:
+            for k in h.keys():
+                index[k] = h
+        lazy = {k: index[k].get_slice(k) for k in index}
+        model.load_hf_state_dict(lazy)
+        return model
+
     def new_cache(self, batch: int, max_len: int, page: int = 64) -> KVCache:
         return KVCache.allocate(self.cfg.num_layers, batch, max_len, self.nkv, self.hd, self.device, self.dtype, page)
 
