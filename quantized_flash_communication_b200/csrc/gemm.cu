@@ -63,6 +63,8 @@ struct Cfg {
   static constexpr uint32_t IDESC = tc::idesc_f16(TILE_M, BN, true);
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
+// EPI_QS*: per epilogue warp, 32 staged rows of one quantized 128-column group.
+constexpr int QS_STAGE_BYTES = 4 * 32 * 256;
 
 // EPI_QS8 / EPI_QS4 / EPI_QS16: quantize each 128-column group of the (bf16-rounded) tile
 // to INT8 / INT4 / raw bf16 and store it into the owner rank's reduce-scatter slot.
@@ -87,16 +89,27 @@ struct GemmArgs {
   ScatterArgs sc;    // EPI_QS*
 };
 
-// Quantize 128 consecutive values of one row (held by this thread) and store the codes
-// plus the group's (scale, zero) into slot / meta.  P = 8, 4 or 16 (raw bf16).
+// Payload bytes of one 128-value group: INT8 codes, packed INT4 codes or raw bf16.
 template <int P>
-QFC_DEV void qs_store_group(const float (&v)[128], char* slot, char* meta, int64_t local, const ScatterArgs& sc) {
+constexpr int qs_group_bytes() { return P == 8 ? 128 : (P == 4 ? 64 : 256); }
+
+// Staging row of one thread: its group's payload, 16-byte chunk c at c ^ (row & 7) (mask
+// 3 for the 4-chunk INT4 rows) so that a warp's rows spread over the banks.
+template <int P>
+QFC_DEV int qs_swz(int row, int c) { return c ^ (row & (P == 4 ? 3 : 7)); }
+
+// Quantize 128 consecutive values of one row (held by this thread): the codes go to the
+// warp's staging row `stage` (shared memory), the group's (scale, zero) straight to meta.
+// P = 8, 4 or 16 (raw bf16).
+template <int P>
+QFC_DEV void qs_encode_group(const float (&v)[128], uint8_t* stage, int srow, char* meta, int64_t local,
+                             const ScatterArgs& sc) {
+  uint4* st = reinterpret_cast<uint4*>(stage);
   if constexpr (P == 16) {
-    uint4* dst = reinterpret_cast<uint4*>(slot + local * 2);
 #pragma unroll
     for (int k = 0; k < 16; ++k)
-      dst[k] = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
-                          pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+      st[qs_swz<P>(srow, k)] = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                                          pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
   } else {
     float mn4[4] = {v[0], v[1], v[2], v[3]}, mx4[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
@@ -112,9 +125,8 @@ QFC_DEV void qs_store_group(const float (&v)[128], char* slot, char* meta, int64
     if (sc.sym) QMath<P, true>::params(mn, mx, s, inv, z);
     else QMath<P, false>::params(mn, mx, s, inv, z);
     if constexpr (P == 8) {
-      uint4* dst = reinterpret_cast<uint4*>(slot + local);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {  // 16 codes per 16-byte store
+      for (int k = 0; k < 8; ++k) {  // 16 codes per 16-byte chunk
         uint32_t m0[8], m1[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -122,12 +134,11 @@ QFC_DEV void qs_store_group(const float (&v)[128], char* slot, char* meta, int64
           m1[i] = QMath<P, false>::codebits(v[16 * k + 8 + i], inv, z);
         }
         const uint2 a = codebits8_to_u2(m0), b = codebits8_to_u2(m1);
-        dst[k] = make_uint4(a.x, a.y, b.x, b.y);
+        st[qs_swz<P>(srow, k)] = make_uint4(a.x, a.y, b.x, b.y);
       }
     } else {
-      uint4* dst = reinterpret_cast<uint4*>(slot + (local >> 1));
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {  // 32 codes per 16-byte store
+      for (int k = 0; k < 4; ++k) {  // 32 codes per 16-byte chunk
         uint32_t w[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -136,13 +147,36 @@ QFC_DEV void qs_store_group(const float (&v)[128], char* slot, char* meta, int64
           for (int i = 0; i < 8; ++i) m[i] = QMath<P, false>::codebits(v[32 * k + 8 * q + i], inv, z);
           w[q] = codebits8_to_int4(m);
         }
-        dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
+        st[qs_swz<P>(srow, k)] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
     const int64_t g = local >> sc.gs_shift;
     if (sc.meta_fp32) *reinterpret_cast<float2*>(meta + g * 8) = make_float2(s, z);
     else *reinterpret_cast<uint32_t*>(meta + g * 4) = pack_f16x2(s, z);
   }
+}
+
+// The warp's 32 staged rows go out row-contiguous: LPR lanes per row, 16 bytes each, so a
+// store instruction writes 512 bytes as a few whole 64- to 256-byte row segments (over
+// NVLink when the owner is a peer) instead of 32 scattered 16-byte pieces.  dst = the
+// row's payload destination (nullptr: row outside the output).
+template <int P>
+QFC_DEV void qs_flush_rows(const uint8_t* stage_warp, char* dst, int lane) {
+  constexpr int PB = qs_group_bytes<P>();
+  constexpr int LPR = PB / 16;
+  constexpr int RPI = 32 / LPR;
+  __syncwarp();
+#pragma unroll 4
+  for (int it = 0; it < 32 / RPI; ++it) {
+    const int rr = it * RPI + lane / LPR, c = lane % LPR;
+    const unsigned long long d =
+        __shfl_sync(QFC_FULL_MASK, (unsigned long long)reinterpret_cast<uintptr_t>(dst), rr);
+    if (d) {
+      const uint4 x = *reinterpret_cast<const uint4*>(stage_warp + rr * PB + (qs_swz<P>(rr, c) << 4));
+      *reinterpret_cast<uint4*>(reinterpret_cast<char*>(d) + c * 16) = x;
+    }
+  }
+  __syncwarp();  // the staging rows are rewritten by the next group
 }
 
 QFC_DEV void tile_coords(int tile, int m_tiles, int n_tiles, int& mb, int& nb) {
@@ -180,6 +214,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   uint64_t* drain = bars + 2 * STAGES + 4;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  uint8_t* qs_stage = reinterpret_cast<uint8_t*>(bars) + 256;  // EPI_QS* only (QS_STAGE_BYTES)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // scheduling unit: a CTA, or a CTA pair (cluster of 2; rank 0 issues the MMAs)
@@ -348,6 +383,8 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
           for (int c = 0; c < 4; ++c) tc::tmem_reg_fence(r[c]);
           const int col = col0 + g0;
+          uint8_t* stage_warp = qs_stage + q * 32 * qs_group_bytes<P>();
+          char* dst = nullptr;
           if (row < args.M && col < args.N) {
             float v[128];
 #pragma unroll
@@ -359,8 +396,10 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             const int owner = (int)(e / args.sc.chunk);
             const int64_t local = e - (int64_t)owner * args.sc.chunk;
             char* slot = args.sc.base[owner] + args.sc.rs_off + (int64_t)args.sc.rank * args.sc.slot1;
-            qs_store_group<P>(v, slot, slot + args.sc.pay1, local, args.sc);
+            qs_encode_group<P>(v, stage_warp + lane * qs_group_bytes<P>(), lane, slot + args.sc.pay1, local, args.sc);
+            dst = slot + (P == 8 ? local : (P == 4 ? (local >> 1) : local * 2));
           }
+          qs_flush_rows<P>(stage_warp, dst, lane);
         }
       } else if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll 1
@@ -536,10 +575,12 @@ int sm_count(int dev) {
 template <int EPI, bool PAIR>
 void launch_cfg(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& a, int M, int dev, int max_ctas) {
   using C = Cfg<PAIR>;
+  constexpr int smem = C::SMEM_BYTES + (is_qs(EPI) ? QS_STAGE_BYTES : 0);
+  static_assert(smem <= 232448, "GEMM shared memory exceeds 227 KiB");
   static bool attr_set[64] = {false};
   auto kern = gemm_bf16_kernel<EPI, PAIR>;
   if (!attr_set[dev]) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr_set[dev] = true;
   }
   const int tiles = ((M + C::TILE_M - 1) / C::TILE_M) * a.n_tiles;
@@ -550,7 +591,7 @@ void launch_cfg(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& a,
   std::memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(units * per_unit);
   cfg.blockDim = dim3(NUM_THREADS);
-  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

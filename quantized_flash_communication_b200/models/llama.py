@@ -18,6 +18,7 @@ residual add, RoPE + paged KV-cache write, attention, embedding and argmax.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Optional
 
@@ -72,7 +73,7 @@ class TPContext:
         # stores 4 KiB apart; from 4 ranks on, most of the tile crosses NVLink that way and
         # the GEMM followed by the standalone all-reduce kernel is faster (measured at 4
         # ranks: 17.7 ms vs 25.6 ms per Llama-2-7B prefill step for o_proj + down_proj).
-        self.fuse_max_world = 2
+        self.fuse_max_world = int(os.environ.get("QFC_FUSE_MAX_WORLD", "2"))
         self.timer = None  # utils.trace.OpTimer shared with the model when attached
         self.ar: Optional[QuantAllReduce] = None
         if self.world > 1 and ar_backend == "qfc":
