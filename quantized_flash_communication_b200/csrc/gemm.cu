@@ -87,6 +87,13 @@ struct GemmArgs {
   int* status;
   uint64_t timeout_ns;
   ScatterArgs sc;    // EPI_QS*
+  // split-K (single CTAs, small M): work unit = (tile, split); each unit writes its fp32
+  // partial tile, the last unit of a tile (device counter) sums them in split order into
+  // TMEM and runs the epilogue.
+  int splits;        // 1 = no split
+  int kb_split;      // k-blocks per split
+  float* part;       // [tiles][splits][BM][BN] fp32
+  int* counters;     // [tiles], zero between launches (the last unit resets its entry)
 };
 
 // Payload bytes of one 128-value group: INT8 codes, packed INT4 codes or raw bf16.
@@ -223,7 +230,9 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   const int m_tiles = (args.M + C::TILE_M - 1) / C::TILE_M;
   const int tiles = m_tiles * args.n_tiles;
+  const int works = tiles * args.splits;
   const int kbs = (args.K + BK - 1) / BK;
+  __shared__ int s_split_last;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -264,11 +273,13 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int last_issue[STAGES];
       for (int s = 0; s < STAGES; ++s) last_issue[s] = -1;
       bool ok = true;
-      for (int tile = unit; tile < tiles && ok; tile += n_units) {
+      for (int w = unit; w < works && ok; w += n_units) {
+        const int tile = w / args.splits, sp = w - tile * args.splits;
+        const int kb0 = sp * args.kb_split, kb1 = min(kbs, kb0 + args.kb_split);
         int mb, nb;
         tile_coords(tile, m_tiles, args.n_tiles, mb, nb);
         const int yb = nb * args.b_first_step;
-        for (int kb = 0; kb < kbs; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!tc::mbar_wait(tc::smem_u32(&empty[s]), ph ^ 1, globaltimer_ns() + args.timeout_ns, s_abort)) {
@@ -309,7 +320,8 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int it = 0, t = 0;
       bool ok = true;
       bool issued = false;
-      for (int tile = unit; tile < tiles && ok; tile += n_units, ++t) {
+      for (int w = unit; w < works && ok; w += n_units, ++t) {
+        const int kb0 = (w % args.splits) * args.kb_split, kb1 = min(kbs, kb0 + args.kb_split);
         const int buf = t & 1;
         if (!tc::mbar_wait(tc::smem_u32(&tempty[buf]), ((t >> 1) & 1) ^ 1, globaltimer_ns() + args.timeout_ns,
                            s_abort)) {
@@ -319,7 +331,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         tc::tc_fence_after();
         const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BN);
-        for (int kb = 0; kb < kbs; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!tc::mbar_wait(tc::smem_u32(&full[s]), ph, globaltimer_ns() + args.timeout_ns, s_abort)) {
@@ -334,10 +346,10 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           for (int k = 0; k < BK / 16; ++k) {
             if constexpr (PAIR)
               tc::umma_f16_pair(tmem_d, tc::sw128_kmajor_desc(a0 + k * 32), tc::sw128_kmajor_desc(b0 + k * 32),
-                                C::IDESC, (kb | k) != 0);
+                                C::IDESC, (kb != kb0) || (k != 0));
             else
               tc::umma_f16(tmem_d, tc::sw128_kmajor_desc(a0 + k * 32), tc::sw128_kmajor_desc(b0 + k * 32), C::IDESC,
-                           (kb | k) != 0);
+                           (kb != kb0) || (k != 0));
           }
           issued = true;
           if constexpr (PAIR) tc::umma_commit_pair(tc::smem_u32(&empty[s]), 0x3);
@@ -360,7 +372,8 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const int q = warp & 3;  // the TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
     int t = 0;
-    for (int tile = unit; tile < tiles; tile += n_units, ++t) {
+    for (int w = unit; w < works; w += n_units, ++t) {
+      const int tile = w / args.splits;
       int mb, nb;
       tile_coords(tile, m_tiles, args.n_tiles, mb, nb);
       const int buf = t & 1;
@@ -372,6 +385,65 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const uint32_t taddr = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
       const int row = mb * C::TILE_M + (int)crank * BM + row_in_tile;
       const int col0 = nb * args.n_tile_cols;
+      if constexpr (!PAIR && !is_qs(EPI)) {
+        if (args.splits > 1) {
+          // this unit's fp32 partial out of TMEM
+          const int S = args.splits, sp = w - tile * S;
+          float* mine = args.part + (((int64_t)tile * S + sp) * BM + row_in_tile) * BN;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t r[32];
+            tc::tmem_ld_32x32b_x32(taddr + c, r);
+            tc::tmem_wait_ld();
+            tc::tmem_reg_fence(r);
+            if (row < args.M) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                reinterpret_cast<uint4*>(mine + c)[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+            }
+          }
+          __threadfence();
+          asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+          if (threadIdx.x == 64) {
+            const int prev = atomicAdd(args.counters + tile, 1);
+            s_split_last = (prev == S - 1);
+            if (prev == S - 1) args.counters[tile] = 0;  // every unit of the tile has arrived
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (!s_split_last) {
+            tc::tc_fence_before();
+            tc::mbar_arrive(tc::smem_u32(&tempty[buf]));
+            continue;
+          }
+          __threadfence();
+          // the sum of all splits, in split order, back into this TMEM buffer
+          const float* p0 = args.part + ((int64_t)tile * S * BM + row_in_tile) * BN;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            float acc[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+            if (row < args.M) {
+              for (int s2 = 0; s2 < S; ++s2) {
+                const float4* src = reinterpret_cast<const float4*>(p0 + (int64_t)s2 * BM * BN + c);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float4 x = __ldcg(src + j);
+                  acc[4 * j] += x.x;
+                  acc[4 * j + 1] += x.y;
+                  acc[4 * j + 2] += x.z;
+                  acc[4 * j + 3] += x.w;
+                }
+              }
+            }
+            uint32_t r[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(acc[j]);
+            tc::tmem_st_32x32b_x32(taddr + c, r);
+          }
+          tc::tmem_wait_st();
+        }
+      }
       if constexpr (is_qs(EPI)) {
         constexpr int P = EPI == EPI_QS8 ? 8 : (EPI == EPI_QS4 ? 4 : 16);
 #pragma unroll 1
@@ -557,6 +629,31 @@ int* status_word() {
   return p;
 }
 
+// Split-K for small M is on unless QFC_GEMM_SPLITK=0 (kept for A/B measurements).
+bool split_k_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("QFC_GEMM_SPLITK");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Per-device arrival counters of split-K tiles, zeroed once; each launch leaves them zero.
+int* split_counters(int dev, int tiles) {
+  constexpr int kMaxTiles = 1 << 14;
+  static int* buf[64] = {nullptr};
+  static std::mutex mu;
+  TORCH_CHECK(tiles <= kMaxTiles, "gemm: too many split-K tiles");
+  std::lock_guard<std::mutex> lock(mu);
+  if (buf[dev] == nullptr) {
+    void* p = nullptr;
+    C10_CUDA_CHECK(cudaMalloc(&p, kMaxTiles * sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(p, 0, kMaxTiles * sizeof(int)));
+    buf[dev] = static_cast<int*>(p);
+  }
+  return buf[dev];
+}
+
 // CTA-pair GEMMs are on unless QFC_GEMM_PAIR=0 (kept for A/B measurements).
 bool pair_enabled() {
   static const bool on = [] {
@@ -585,7 +682,28 @@ void launch_cfg(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& a,
   }
   const int tiles = ((M + C::TILE_M - 1) / C::TILE_M) * a.n_tiles;
   const int per_unit = PAIR ? 2 : 1;
-  int units = std::min(tiles, sm_count(dev) / per_unit);
+  GemmArgs args = a;
+  args.splits = 1;
+  args.kb_split = (a.K + BK - 1) / BK;
+  args.part = nullptr;
+  args.counters = nullptr;
+  at::Tensor part;
+  const int kbs = (a.K + BK - 1) / BK;
+  if (!PAIR && !is_qs(EPI) && split_k_enabled() && 2 * tiles <= sm_count(dev) && kbs >= 8 && max_ctas <= 0) {
+    // small M: too few tiles to stream the weights from every SM; split K so that about
+    // one unit per SM runs, each with at least 4 k-blocks
+    int S = std::min(sm_count(dev) / tiles, kbs / 4);
+    if (S > 1) {
+      args.kb_split = (kbs + S - 1) / S;
+      args.splits = (kbs + args.kb_split - 1) / args.kb_split;
+      part = at::empty({(int64_t)tiles * args.splits * BM * BN},
+                       at::TensorOptions().dtype(at::kFloat).device(at::kCUDA, dev));
+      args.part = part.data_ptr<float>();
+      args.counters = split_counters(dev, tiles);
+    }
+  }
+  const int works = tiles * args.splits;
+  int units = std::min(works, sm_count(dev) / per_unit);
   if (max_ctas > 0) units = std::min(units, std::max(1, max_ctas / per_unit));
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
@@ -600,7 +718,7 @@ void launch_cfg(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& a,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = PAIR ? 1 : 0;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tA, tB, a));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tA, tB, args));
 }
 
 // CTA pairs serve M >= 256 (a 256-row tile per pair); smaller M runs one CTA per tile.
@@ -630,6 +748,10 @@ void launch(const at::Tensor& A, const at::Tensor& B, at::Tensor* D, const at::T
   a.ldr = R ? (int)R->stride(0) : 0;
   a.status = status_word();
   a.timeout_ns = (uint64_t)(timeout_ms * 1e6);
+  a.splits = 1;
+  a.kb_split = (K + BK - 1) / BK;
+  a.part = nullptr;
+  a.counters = nullptr;
   const CUtensorMap tA = make_tmap(A.data_ptr(), M, K, A.stride(0), BM);
   const CUtensorMap tB = make_tmap(B.data_ptr(), B.size(0), K, B.stride(0), 128);
   const bool pair = M >= 2 * BM && pair_enabled() && (max_ctas <= 0 || max_ctas >= 2);

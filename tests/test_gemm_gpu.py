@@ -50,6 +50,26 @@ def test_gemm_residual_in_place(cuda_device):
     assert torch.allclose(r.float(), ref, rtol=2e-2, atol=3e-2)
 
 
+@pytest.mark.parametrize("M,N,K", [(50, 1024, 2048), (128, 512, 4096), (7, 4096, 14336)])
+def test_gemm_split_k_small_m(cuda_device, M, N, K):
+    """Few tiles and a long K: the GEMM splits K; plain and residual epilogues, run twice
+    (the arrival counters must be back to zero after a launch)."""
+    a = torch.randn(M, K, device=cuda_device, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=cuda_device, dtype=torch.bfloat16) * 0.02
+    r = torch.randn(M, N, device=cuda_device, dtype=torch.bfloat16)
+    ref = _ref(a, w)
+    for _ in range(2):
+        y = G.linear(a, w)
+        torch.cuda.synchronize()
+        assert G.gemm_status() == 0
+        assert torch.allclose(y.float(), ref, rtol=2e-2, atol=2e-2)
+        out = r.clone()
+        G.linear_residual(a, w, out, out=out)
+        assert torch.allclose(out.float(), ref + r.float(), rtol=2e-2, atol=3e-2)
+    y2 = G.linear(a, w)
+    assert torch.equal(y, y2)  # the split order is fixed: deterministic
+
+
 def test_gemm_persistent_small_grid(cuda_device):
     from quantized_flash_communication_b200._ext import ext
     a = torch.randn(1024, 1024, device=cuda_device, dtype=torch.bfloat16)
