@@ -599,14 +599,18 @@ class GraphedStep:
 
 
 def smoke_forward(device) -> None:
-    """One tiny prefill + decode step of the flagship architecture (random weights)."""
+    """One tiny prefill + decode step of the flagship architecture (random weights).
+
+    GQA (8 query / 2 kv heads) and 4 x 64 prompt tokens, so the step runs the CTA-pair
+    GEMMs (256 rows), the tcgen05 prefill attention, the split-K GEMMs and the tensor-core
+    decode attention."""
     from .config import LlamaConfig
-    cfg = LlamaConfig("smoke", 1024, 2048, 1, 8, 8, 1024, head_dim=128, max_position=512)
+    cfg = LlamaConfig("smoke", 1024, 2048, 1, 8, 2, 1024, head_dim=128, max_position=512)
     m = LlamaTP(cfg, device=device)
-    ids = torch.randint(0, cfg.vocab_size, (2, 64), device=device)
-    cache = m.new_cache(2, 80)
+    ids = torch.randint(0, cfg.vocab_size, (4, 64), device=device)
+    cache = m.new_cache(4, 80)
     tok = m.prefill(ids, cache)
     tok2 = m.decode_step(tok, cache)
     torch.cuda.synchronize(device)
-    assert tok.shape == (2,) and tok2.shape == (2,)
+    assert tok.shape == (4,) and tok2.shape == (4,)
     assert G.gemm_status() == 0
