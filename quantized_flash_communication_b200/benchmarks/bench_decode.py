@@ -50,6 +50,8 @@ def main(argv=None):
     ap.add_argument("--ar-backend", default="qfc", choices=["qfc", "nccl"])
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (debug only)")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="also time eager decode steps per operator (CUDA-event regions, max over ranks)")
     args = ap.parse_args(argv)
     rank, world, dev = init_distributed()
     cfg = get_config(args.model)
@@ -59,7 +61,7 @@ def main(argv=None):
     tp = TPContext(None, dev, ar_backend=args.ar_backend, bits=args.bits, group_size=args.group_size,
                    reserve_tokens=B * S, hidden_size=cfg.hidden_size)
     model = LlamaTP(cfg, tp, dev, init="shard", seed=7)
-    cache = model.new_cache(B, S + args.new + args.warmup + 1)
+    cache = model.new_cache(B, S + args.new + args.warmup + 1 + (8 if args.breakdown else 0))
     ids = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(1)).to(dev)
     model.prefill(ids, cache)  # warm-up (JIT-free kernels; sizes the workspaces)
     torch.cuda.synchronize()
@@ -92,12 +94,27 @@ def main(argv=None):
     if tp.ar is not None:
         tp.ar.check()
     step.release()
+    breakdown = None
+    if args.breakdown:
+        from ..utils.trace import OpTimer
+        timer = OpTimer()
+        model.timer = tp.timer = timer
+        for _ in range(4):
+            cur = model.decode_step(cur, cache)
+        summ = timer.summary()
+        model.timer = tp.timer = None
+        names = list(summ)
+        vals = torch.tensor([summ[k]["ms"] / 4 for k in names], dtype=torch.float64, device=dev)
+        if dist.is_available() and dist.is_initialized():
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        breakdown = {k: round(float(v), 4) for k, v in zip(names, vals.tolist())}
     if rank == 0:
         print(json.dumps({
             "benchmark": "tp_decode", "model": cfg.name, "n_gpus": world, "batch": B, "ctx": S, "new_tokens": args.new,
             "allreduce": f"{args.ar_backend} INT{args.bits} g{args.group_size}" if world > 1 else "none (tp1)",
             "ttft_ms": ttft, "per_token_ms": per_tok, "decode_tokens_per_s": B * 1000.0 / per_tok,
             "launch": "cuda_graph", "clocks": sampler.summary() if sampler else None,
+            "eager_breakdown_ms_per_token": breakdown,
             "data": "synthetic: uniform random token ids, random-init N(0,0.02) weights"}), flush=True)
     reset_communicators()
     if dist.is_available() and dist.is_initialized():

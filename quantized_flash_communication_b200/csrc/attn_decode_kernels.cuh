@@ -118,7 +118,7 @@ decode_partial_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T
   const int b = blockIdx.z, kvh = blockIdx.y, part = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sub = lane % LPT, tg = lane / LPT;
-  const int L = seq_lens[b];
+  const int L = min(seq_lens[b], max_pages << page_shift);  // never past the block table
   const int t0 = part * part_tok;
   const int t1 = min(L, t0 + part_tok);
   const int n_st = t1 > t0 ? (t1 - t0 + kStageTok - 1) / kStageTok : 0;
@@ -370,7 +370,7 @@ decode_partial_mma_kernel(const T* __restrict__ q, const T* __restrict__ kc, con
   const int b = blockIdx.z, kvh = blockIdx.y, part = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;  // mma group row / thread-in-group
-  const int L = seq_lens[b];
+  const int L = min(seq_lens[b], max_pages << page_shift);  // never past the block table
   const int t0 = part * part_tok;
   const int t1 = min(L, t0 + part_tok);
   const int n_st = t1 > t0 ? (t1 - t0 + kMmaStageTok - 1) / kMmaStageTok : 0;

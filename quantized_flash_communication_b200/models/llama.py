@@ -163,9 +163,18 @@ class KVCache:
         bt = torch.arange(pages, device=device, dtype=torch.int32).view(batch, pps)
         return KVCache(k, v, bt, torch.zeros(batch, device=device, dtype=torch.int32), page)
 
+    @property
+    def capacity(self) -> int:
+        """Tokens per sequence the block table can hold."""
+        return self.block_table.shape[1] * self.page
+
     def slots(self, b_idx: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
-        pg = self.block_table[b_idx, (pos // self.page).to(torch.long)].to(torch.int64)
-        return pg * self.page + (pos % self.page).to(torch.int64)
+        """Cache slot of each (sequence, position); -1 (not cached) past the capacity, so a
+        step past the end never indexes outside the block table."""
+        pidx = (pos // self.page).to(torch.long).clamp(max=self.block_table.shape[1] - 1)
+        pg = self.block_table[b_idx, pidx].to(torch.int64)
+        slot = pg * self.page + (pos % self.page).to(torch.int64)
+        return torch.where(pos < self.capacity, slot, torch.full_like(slot, -1))
 
 
 # ------------------------------------------------------------------------------------------
@@ -501,11 +510,14 @@ class LlamaTP(nn.Module):
         """One token per sequence: appends to the cache and returns greedy next tokens [B]."""
         B = tokens.numel()
         cfg = self.cfg
-        pos = cache.seq_lens.to(torch.int64)
-        b_idx = torch.arange(B, device=self.device)
-        slots = cache.slots(b_idx, pos)
-        h = L.embedding(tokens.reshape(-1), self.model.embed_tokens.weight)
-        x = L.rmsnorm(h, self.model.layers[0].input_layernorm.weight, cfg.rms_eps)
+        t = self.timer
+        with maybe_region(t, "positions+slots"):
+            pos = cache.seq_lens.to(torch.int64)
+            b_idx = torch.arange(B, device=self.device)
+            slots = cache.slots(b_idx, pos)
+        with maybe_region(t, "embedding+rmsnorm"):
+            h = L.embedding(tokens.reshape(-1), self.model.embed_tokens.weight)
+            x = L.rmsnorm(h, self.model.layers[0].input_layernorm.weight, cfg.rms_eps)
         cache.seq_lens.add_(1)
         nqr = self.nq * self.hd
 
@@ -516,7 +528,8 @@ class LlamaTP(nn.Module):
 
         for li in range(cfg.num_layers):
             x = self._layer(li, h, x, attn, pos, slots, cache)
-        return self._head(x)
+        with maybe_region(t, "lm_head+argmax"):
+            return self._head(x)
 
     @torch.no_grad()
     def capture_prefill(self, batch: int, seq: int, cache: Optional[KVCache] = None,
@@ -571,6 +584,8 @@ class LlamaTP(nn.Module):
         B, S = ids.shape
         if cache is None:
             cache = self.new_cache(B, S + max_new_tokens)
+        if S + max_new_tokens - 1 > cache.capacity:
+            raise ValueError(f"cache holds {cache.capacity} tokens per sequence; {S} + {max_new_tokens} requested")
         out = torch.empty(B, max_new_tokens, dtype=torch.int64, device=self.device)
         tok = self.prefill(ids, cache)
         out[:, 0] = tok
