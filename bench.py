@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-Llama-2-7B architecture (32 layers, hidden 4096, 32 heads, SwiGLU
+The flagship configuration: Llama-2-7B architecture (32 layers, hidden 4096, 32 heads, SwiGLU
 11008, vocab 32000), bf16 random-init N(0, 0.02) weights, batch 8 x 1024 uniformly random
 token ids, an INT8 (group 128) quantized all-reduce after o_proj and down_proj.  One step
 is one prefill of the whole batch up to the first generated token (TTFT); ``value`` is

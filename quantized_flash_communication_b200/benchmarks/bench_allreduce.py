@@ -1,4 +1,4 @@
-"""All-reduce sweep (BASELINE config 2): fused quantized all-reduce vs NCCL bf16.
+"""All-reduce sweep: fused quantized all-reduce vs NCCL bf16.
 
     torchrun --nproc-per-node N -m quantized_flash_communication_b200.benchmarks.bench_allreduce \
         [--tokens 1,16,128,1024,4096,16384] [--hidden 4096,8192] [--bits 8,4] [--gs 32,64,128] [--reference]

@@ -1,4 +1,4 @@
-"""Prefill + decode benchmark (BASELINE configs 4 and 5).
+"""Prefill + decode benchmark (Llama-3-8B at TP 2/4/8, Llama-3-70B at TP 8).
 
     torchrun --nproc-per-node N -m quantized_flash_communication_b200.benchmarks.bench_decode \
         --model llama3-8b --batch 64 --ctx 4096 --new 128 --bits 8

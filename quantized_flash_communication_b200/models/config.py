@@ -1,4 +1,4 @@
-"""Llama-family architecture configs (the shapes BASELINE names, plus the reference's model)."""
+"""Llama-family architecture configs (the benchmarked shapes, plus the reference's model)."""
 from __future__ import annotations
 
 from dataclasses import dataclass, field, replace
@@ -50,11 +50,11 @@ class LlamaConfig:
 
 
 PRESETS = {
-    # Llama-2-7B (MHA, SwiGLU 11008, vocab 32000)
+    # prefill benchmark: Llama-2-7B (MHA, SwiGLU 11008, vocab 32000)
     "llama2-7b": LlamaConfig("llama2-7b", 4096, 11008, 32, 32, 32, 32000, rope_theta=10000.0, max_position=4096),
-    # Llama-3-8B (GQA 32/8, SwiGLU 14336, vocab 128256)
+    # decode benchmark: Llama-3-8B (GQA 32/8, SwiGLU 14336, vocab 128256)
     "llama3-8b": LlamaConfig("llama3-8b", 4096, 14336, 32, 32, 8, 128256, rope_theta=500000.0, max_position=8192),
-    # Llama-3-70B (GQA 64/8, SwiGLU 28672)
+    # prefill + decode benchmark at TP 8: Llama-3-70B (GQA 64/8, SwiGLU 28672)
     "llama3-70b": LlamaConfig("llama3-70b", 8192, 28672, 80, 64, 8, 128256, rope_theta=500000.0, max_position=8192),
     # The reference's model (main.py:190): Llama-3.2-3B-Instruct
     "llama3.2-3b": LlamaConfig("llama3.2-3b", 3072, 8192, 28, 24, 8, 128256, rope_theta=500000.0,

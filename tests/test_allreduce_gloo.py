@@ -1,6 +1,6 @@
 """Two-step quantized all-reduce on CPU / gloo ranks (no GPU).
 
-world_size 2, each rank holds fp32 [8, 4096] drawn N(0,1) from
+The gloo configuration: world_size 2, each rank holds fp32 [8, 4096] drawn N(0,1) from
 seed+rank; symmetric groups of 128 with fp32 absmax scales; INT8 and INT4 (nibble
 packed); checked against the exact fp32 sum by relative L2 and bit-for-bit against the
 single-process oracle.
