@@ -44,6 +44,8 @@ def _parse():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch kernels eagerly instead of one CUDA graph")
+    ap.add_argument("--seq-parallel", action="store_true",
+                    help="sequence-parallel residual stream: the all-reduces also add the residual and normalise")
     ap.add_argument("--breakdown", action="store_true",
                     help="print per-operator device times of eager steps instead of the benchmark line")
     ap.add_argument("--no-fuse-gemm", action="store_true",
@@ -177,7 +179,7 @@ def run_ours(args):
     B, S = args.batch, args.seq
     tp = TPContext(None, dev, ar_backend=args.ar_backend, bits=args.bits, group_size=args.group_size,
                    quant_type=args.quant_type, algo="auto", reserve_tokens=B * S, hidden_size=cfg.hidden_size,
-                   fuse_gemm=not args.no_fuse_gemm)
+                   fuse_gemm=not args.no_fuse_gemm, seq_parallel=args.seq_parallel or None)
     model = LlamaTP(cfg, tp, dev, init="shard", seed=1234)
     g = torch.Generator(device="cpu").manual_seed(42)
     ids_host = torch.randint(0, cfg.vocab_size, (B, S), generator=g).pin_memory()
@@ -245,6 +247,8 @@ def run_ours(args):
                    "allreduce": (f"qfc INT{args.bits} g{args.group_size} {args.quant_type}"
                                  + (", scatter fused into o/down GEMM epilogues"
                                     if tp.fuse_gemm and world <= tp.fuse_max_world else "")
+                                 + (", sequence-parallel residual + RMSNorm in the all-reduce"
+                                    if tp.sp_active(B * S, cfg.hidden_size) else "")
                                  if args.ar_backend == "qfc" else args.ar_backend) if world > 1 else "none (tp1)",
                    "attention": A.prefill_backend(),
                    "launch": "cuda_graph" if graphed is not None else "eager",

@@ -29,6 +29,15 @@ void quant_all_reduce(const std::vector<std::shared_ptr<Workspace>>& wss, const 
                       bool one_shot, bool quantize_local, double timeout_ms);
 void gemm_all_reduce(const std::shared_ptr<Workspace>& ws, const at::Tensor& a, const at::Tensor& w, at::Tensor& out,
                      int64_t bits, int64_t gs, bool sym, bool scale_fp32, double timeout_ms);
+// allreduce_norm.cu
+std::vector<int64_t> ar_plan_rows(int64_t M, int64_t H, int64_t world, int64_t bits, bool scale_fp32);
+void quant_all_reduce_norm(const std::vector<std::shared_ptr<Workspace>>& wss, const std::vector<at::Tensor>& partials,
+                           const std::vector<at::Tensor>& hs, const at::Tensor& weight,
+                           const std::vector<at::Tensor>& xs, int64_t bits, bool sym, bool scale_fp32,
+                           bool quantize_local, double eps, double timeout_ms);
+void gemm_all_reduce_norm(const std::shared_ptr<Workspace>& ws, const at::Tensor& a, const at::Tensor& w,
+                          const at::Tensor& h, const at::Tensor& weight, at::Tensor& x, int64_t bits, bool sym,
+                          bool scale_fp32, double eps, double timeout_ms);
 // gemm.cu
 at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& out, int64_t epi,
                      const c10::optional<at::Tensor>& residual, double timeout_ms, int64_t max_ctas);
@@ -108,4 +117,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "all_reduce(a @ w^T) with the quantize-and-scatter fused into the GEMM epilogue", py::arg("workspace"),
         py::arg("a"), py::arg("w"), py::arg("out"), py::arg("bits"), py::arg("group_size"), py::arg("sym"),
         py::arg("scale_fp32"), py::arg("timeout_ms"));
+  m.def("ar_plan_rows", &qfc::ar_plan_rows, "region sizes of a row-blocked (sequence-parallel) all-reduce + norm");
+  m.def("quant_all_reduce_norm", &qfc::quant_all_reduce_norm,
+        "x = all_gather(rmsnorm(h_shard += reduce_scatter(partial)) * w), one kernel over peer memory",
+        py::arg("workspaces"), py::arg("partials"), py::arg("residual_shards"), py::arg("weight"), py::arg("outs"),
+        py::arg("bits"), py::arg("sym"), py::arg("scale_fp32"), py::arg("quantize_local"), py::arg("eps"),
+        py::arg("timeout_ms"));
+  m.def("gemm_all_reduce_norm", &qfc::gemm_all_reduce_norm,
+        "the same with the reduce-scatter fused into the row-parallel GEMM's epilogue", py::arg("workspace"),
+        py::arg("a"), py::arg("w"), py::arg("residual_shard"), py::arg("weight"), py::arg("out"), py::arg("bits"),
+        py::arg("sym"), py::arg("scale_fp32"), py::arg("eps"), py::arg("timeout_ms"));
 }

@@ -50,7 +50,7 @@ class TPContext:
     def __init__(self, group: Optional[dist.ProcessGroup] = None, device=None, ar_backend: str = "qfc",
                  bits: int = 8, group_size: int = 128, quant_type: str = "asym", algo: str = "auto",
                  reserve_tokens: int = 0, hidden_size: int = 0, world: Optional[int] = None,
-                 rank: Optional[int] = None, fuse_gemm: bool = True):
+                 rank: Optional[int] = None, fuse_gemm: bool = True, seq_parallel: Optional[bool] = None):
         self.group = group
         if world is not None:  # explicit (e.g. building one shard offline); no communication
             self.world, self.rank = world, rank or 0
@@ -81,6 +81,39 @@ class TPContext:
                                      algo=algo)
             if reserve_tokens and hidden_size:
                 self.ar.reserve(reserve_tokens * hidden_size, torch.bfloat16, bits_options=(bits, 16))
+        # Sequence-parallel residual stream for prefill: each rank keeps rows
+        # [r*R, (r+1)*R) of the residual and the row-parallel all-reduces also add the
+        # residual and apply the next RMSNorm on those rows (csrc/allreduce_norm.cuh), so
+        # only the normalised activations are all-gathered.  Off unless requested
+        # (seq_parallel=True or QFC_SEQ_PARALLEL=1).
+        if seq_parallel is None:
+            seq_parallel = os.environ.get("QFC_SEQ_PARALLEL", "0") == "1"
+        self.seq_parallel = bool(seq_parallel) and self.ar is not None and group_size == 128
+        if self.seq_parallel and reserve_tokens and hidden_size:
+            self.ar.reserve_rows(reserve_tokens, hidden_size, bits_options=(bits, 16))
+
+    def sp_active(self, rows: int, hidden: int) -> bool:
+        """Whether a step of ``rows`` tokens runs with the sequence-parallel residual."""
+        return (self.seq_parallel and self.ar is not None and self.ar_backend == "qfc" and self.group_size == 128
+                and rows >= self.fuse_min_rows and hidden % 256 == 0)
+
+    def sp_rows(self, rows: int):
+        """(rows per rank R, first row, rows owned) of this rank's residual shard."""
+        R = (rows + self.world - 1) // self.world
+        lo = self.rank * R
+        return R, lo, max(0, min(rows, lo + R) - lo)
+
+    def linear_all_reduce_norm(self, x: torch.Tensor, w: torch.Tensor, h_shard: torch.Tensor,
+                               norm_w: torch.Tensor, eps: float) -> torch.Tensor:
+        """Sequence-parallel ``h_shard += all_reduce(x @ w.T)`` (own rows) and the full
+        ``rmsnorm(h) * norm_w`` of every row, gathered from the row owners."""
+        if (self.world <= self.fuse_max_world and self.fuse_gemm and w.shape[0] % 128 == 0):
+            return self.ar.gemm_all_reduce_norm(x, w, h_shard, norm_w, eps, bits=self.bits,
+                                                quant_type=self.quant_type)
+        with maybe_region(self.timer, "  (gemm part)"):
+            p = G.linear(x, w)
+        with maybe_region(self.timer, "  (allreduce+norm part)"):
+            return self.ar.all_reduce_norm(p, h_shard, norm_w, eps, bits=self.bits, quant_type=self.quant_type)
 
     def configure(self, bits: Optional[int] = None, group_size: Optional[int] = None,
                   quant_type: Optional[str] = None, backend: Optional[str] = None):
@@ -401,8 +434,10 @@ class LlamaTP(nn.Module):
     def new_cache(self, batch: int, max_len: int, page: int = 64) -> KVCache:
         return KVCache.allocate(self.cfg.num_layers, batch, max_len, self.nkv, self.hd, self.device, self.dtype, page)
 
-    def _layer(self, li: int, h: torch.Tensor, x: torch.Tensor, attn_fn, pos, slots, cache: Optional[KVCache]):
-        """One decoder layer.  h: residual stream [M, H] (updated in place); x: its norm.
+    def _layer(self, li: int, h: torch.Tensor, x: torch.Tensor, attn_fn, pos, slots, cache: Optional[KVCache],
+               sp: bool = False):
+        """One decoder layer.  h: residual stream [M, H] (updated in place; with ``sp`` only
+        this rank's row shard [R, H]); x: its norm [M, H].
 
         Returns the input norm of the next layer (or the final norm after the last one).
         """
@@ -418,7 +453,11 @@ class LlamaTP(nn.Module):
             L.rope_kv(qkv, pos, self.cos_sin, self.nq, self.nkv, self.hd, kc, vc, slots)
         with maybe_region(t, "attention"):
             o = attn_fn(qkv, li)
-        if tp.world == 1:
+        if sp:
+            with maybe_region(t, "o_proj_gemm+allreduce+norm"):
+                x = tp.linear_all_reduce_norm(o, lay.self_attn.o_proj.weight, h, lay.post_attention_layernorm.weight,
+                                              eps)
+        elif tp.world == 1:
             with maybe_region(t, "o_proj_gemm"):
                 G.linear_residual(o, lay.self_attn.o_proj.weight, h, out=h)
             with maybe_region(t, "rmsnorm"):
@@ -431,6 +470,9 @@ class LlamaTP(nn.Module):
         with maybe_region(t, "gate_up_gemm_swiglu"):
             act = G.linear_swiglu(x, lay.mlp.gate_up_fused)
         nxt = (self.model.layers[li + 1].input_layernorm.weight if li + 1 < cfg.num_layers else self.model.norm.weight)
+        if sp:
+            with maybe_region(t, "down_gemm+allreduce+norm"):
+                return tp.linear_all_reduce_norm(act, lay.mlp.down_proj.weight, h, nxt, eps)
         if tp.world == 1:
             with maybe_region(t, "down_gemm"):
                 G.linear_residual(act, lay.mlp.down_proj.weight, h, out=h)
@@ -481,12 +523,18 @@ class LlamaTP(nn.Module):
         if cache is not None:
             slots = cache.slots(torch.arange(B, device=self.device).repeat_interleave(S), pos)
         x = L.rmsnorm(h, self.model.layers[0].input_layernorm.weight, self.cfg.rms_eps)
+        sp = self.tp.sp_active(B * S, self.cfg.hidden_size)
+        if sp:  # keep only this rank's rows of the residual stream
+            R, lo, n = self.tp.sp_rows(B * S)
+            shard = torch.zeros(R, self.cfg.hidden_size, device=h.device, dtype=h.dtype)
+            shard[:n] = h[lo:lo + n]
+            h = shard
 
         def attn(qkv, li):
             return A.prefill_attention(qkv, B, S, self.nq, self.nkv, self.hd)
 
         for li in range(self.cfg.num_layers):
-            x = self._layer(li, h, x, attn, pos, slots, cache)
+            x = self._layer(li, h, x, attn, pos, slots, cache, sp=sp)
         if cache is not None:
             cache.seq_lens.fill_(S)
         return x

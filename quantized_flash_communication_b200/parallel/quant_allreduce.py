@@ -65,6 +65,10 @@ class _Base:
         _, need_rs, need_ag, need_os = ext().ar_plan(n, W, bits, gs, fp32, elem, one_shot)
         return need_rs, need_ag, need_os
 
+    def _plan_rows(self, M: int, H: int, W: int, bits: int, fp32: bool):
+        _, need_rs, need_ag, need_os = ext().ar_plan_rows(M, H, W, bits, fp32)
+        return need_rs, need_ag, need_os
+
 
 class QuantAllReduce(_Base):
     """Fused quantized all-reduce for one process group (one rank per GPU).
@@ -117,6 +121,56 @@ class QuantAllReduce(_Base):
         self.ws.ensure(*self._plan(x.numel(), self.world, x.element_size(), bits, gs, fp32, one))
         ext().quant_all_reduce([self.ws.native], [x], [out], bits, gs, qt == "sym", fp32, one,
                                self.quantize_local, self.timeout_ms)
+        return out
+
+    def reserve_rows(self, max_rows: int, hidden: int, bits_options: Sequence[int] = (16, 8, 6, 4)):
+        """Size the workspace for row-blocked all-reduce + norm calls of up to ``max_rows``
+        rows of ``hidden`` (call before graph capture)."""
+        fp32 = self.scale_dtype == torch.float32
+        rs = ag = 0
+        for b in bits_options:
+            r, a, _ = self._plan_rows(max_rows, hidden, self.world, b, fp32)
+            rs, ag = max(rs, r), max(ag, a)
+        self.ws.ensure(rs, ag, 0)
+
+    def all_reduce_norm(self, partial: torch.Tensor, residual_shard: torch.Tensor, weight: torch.Tensor, eps: float,
+                        out: Optional[torch.Tensor] = None, bits: Optional[int] = None,
+                        quant_type: Optional[str] = None) -> torch.Tensor:
+        """Sequence-parallel all-reduce + residual + RMSNorm of a row-parallel layer.
+
+        ``partial [M, H]`` is this rank's partial sum; this rank owns rows
+        ``[r*R, (r+1)*R)`` (``R = ceil(M / world)``) of the residual stream, held in
+        ``residual_shard [R, H]`` and updated in place (``h += sum``).  Returns
+        ``x [M, H] = all_gather(rmsnorm(h) * weight)`` (quantized on the wire), identical
+        on every rank.  Group size 128, bf16.
+        """
+        bits = self.bits if bits is None else bits
+        qt = self.quant_type if quant_type is None else quant_type
+        partial = _aligned(partial)
+        M, H = partial.shape
+        if out is None:
+            out = torch.empty(M, H, dtype=torch.bfloat16, device=partial.device)
+        fp32 = self.scale_dtype == torch.float32
+        self.ws.ensure(*self._plan_rows(M, H, self.world, bits, fp32))
+        ext().quant_all_reduce_norm([self.ws.native], [partial], [residual_shard], weight, [out], bits, qt == "sym",
+                                    fp32, self.quantize_local, float(eps), self.timeout_ms)
+        return out
+
+    def gemm_all_reduce_norm(self, a: torch.Tensor, w: torch.Tensor, residual_shard: torch.Tensor,
+                             weight: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None,
+                             bits: Optional[int] = None, quant_type: Optional[str] = None) -> torch.Tensor:
+        """``all_reduce_norm(a @ w.T, ...)`` with the reduce-scatter fused into the GEMM
+        epilogue (every 128-column group of a tile goes to its row owner's slot)."""
+        bits = self.bits if bits is None else bits
+        qt = self.quant_type if quant_type is None else quant_type
+        a2 = a.reshape(-1, a.shape[-1])
+        M, H = a2.shape[0], w.shape[0]
+        if out is None:
+            out = torch.empty(M, H, dtype=torch.bfloat16, device=a.device)
+        fp32 = self.scale_dtype == torch.float32
+        self.ws.ensure(*self._plan_rows(M, H, self.world, bits, fp32))
+        ext().gemm_all_reduce_norm(self.ws.native, a2, w, residual_shard, weight, out, bits, qt == "sym", fp32,
+                                   float(eps), self.timeout_ms)
         return out
 
     def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
@@ -176,3 +230,19 @@ class EmulatedQuantAllReduce(_Base):
 
     def check(self, synchronize: bool = True):
         self.ws.check(synchronize)
+
+    def all_reduce_norm(self, partials: List[torch.Tensor], residual_shards: List[torch.Tensor],
+                        weight: torch.Tensor, eps: float, bits: Optional[int] = None,
+                        quant_type: Optional[str] = None) -> List[torch.Tensor]:
+        """All W ranks of :meth:`QuantAllReduce.all_reduce_norm` in one launch."""
+        assert len(partials) == self.world == len(residual_shards)
+        bits = self.bits if bits is None else bits
+        qt = self.quant_type if quant_type is None else quant_type
+        partials = [_aligned(x) for x in partials]
+        M, H = partials[0].shape
+        outs = [torch.empty(M, H, dtype=torch.bfloat16, device=x.device) for x in partials]
+        fp32 = self.scale_dtype == torch.float32
+        self.ws.ensure(*self._plan_rows(M, H, self.world, bits, fp32))
+        ext().quant_all_reduce_norm(self.ws.all, partials, list(residual_shards), weight, outs, bits, qt == "sym",
+                                    fp32, self.quantize_local, float(eps), self.timeout_ms)
+        return outs

@@ -257,6 +257,39 @@ def one_shot_all_reduce_ref(xs: Sequence[torch.Tensor], bits: int = 8, group_siz
     return acc.to(out_dtype).view(xs[0].shape)
 
 
+def two_step_all_reduce_norm_ref(partials: Sequence[torch.Tensor], residual_shards: Sequence[torch.Tensor],
+                                 weight: torch.Tensor, eps: float, bits: int = 8, group_size: int = 128,
+                                 mode: str = "asym", scale_dtype=torch.float16):
+    """Sequence-parallel all-reduce + residual + RMSNorm as the fused kernel computes it.
+
+    Rank r owns rows ``[r*R, (r+1)*R)`` (``R = ceil(M/W)``) and holds them in
+    ``residual_shards[r] [R, H]``.  ``sum = sum_j dq(q_p1(partial_j))`` (fp32, j in order);
+    ``h = bf16(bf16(sum) + h)``; ``y = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * w)``;
+    every rank receives ``x = dq(q_p2(y))``.  Returns ``(x [M, H] bf16, new shards)``.
+    """
+    W = len(partials)
+    M, H = partials[0].shape
+    R = (M + W - 1) // W
+    p1, p2 = phase_bits(bits)
+    acc = None
+    for x in partials:
+        d = _qdq(x, p1, group_size, mode, scale_dtype).float()
+        acc = d if acc is None else acc + d
+    s_b = acc.view(M, H).to(torch.bfloat16).float()
+    h = torch.cat([t.float() for t in residual_shards], 0)[:M]
+    h = (s_b + h).to(torch.bfloat16).float()
+    rstd = torch.rsqrt((h * h).sum(-1, keepdim=True) / H + eps)
+    y = ((h * rstd).to(torch.bfloat16).float() * weight.float()).to(torch.bfloat16)
+    x = _qdq(y, p2, group_size, mode, scale_dtype).view(M, H).to(torch.bfloat16) if p2 != 16 else y
+    new = []
+    for r in range(W):
+        t = residual_shards[r].clone()
+        n = max(0, min(M, (r + 1) * R) - r * R)
+        t[:n] = h[r * R:r * R + n].to(t.dtype)
+        new.append(t)
+    return x.view(M, H), new
+
+
 def rel_l2(a: torch.Tensor, b: torch.Tensor) -> float:
     a = a.double().reshape(-1)
     b = b.double().reshape(-1)

@@ -142,6 +142,52 @@ def test_gemm_fused_scatter_single_rank(cuda_device, bits, mode):
         assert torch.equal(fused.cpu(), ref)
 
 
+@pytest.mark.parametrize("W,M,H,bits,mode", [(2, 256, 1024, 8, "asym"), (4, 1000, 4096, 8, "asym"),
+                                               (8, 300, 2048, 4, "sym"), (3, 77, 512, 6, "asym"),
+                                               (2, 64, 256, 16, "asym"), (1, 130, 1024, 8, "asym")])
+def test_emulated_all_reduce_norm(cuda_device, W, M, H, bits, mode):
+    """Sequence-parallel all-reduce + residual + RMSNorm: residual shards bit-exact with the
+    oracle, x identical on every rank and equal to the oracle up to rsqrt rounding."""
+    from quantized_flash_communication_b200.parallel import EmulatedQuantAllReduce
+    torch.manual_seed(M + H + bits)
+    ar = EmulatedQuantAllReduce(W, cuda_device, bits=bits, group_size=128, quant_type=mode, algo="two_shot")
+    R = (M + W - 1) // W
+    ps = [torch.randn(M, H, device=cuda_device).to(torch.bfloat16) for _ in range(W)]
+    hs = [torch.randn(R, H, device=cuda_device).to(torch.bfloat16) for _ in range(W)]
+    w = (torch.rand(H, device=cuda_device) + 0.5).to(torch.bfloat16)
+    hs_in = [h.cpu().clone() for h in hs]
+    for rep in range(2):
+        xs = ar.all_reduce_norm(ps, hs, w, 1e-5)
+        ar.check()
+        x_ref, h_ref = spec.two_step_all_reduce_norm_ref([p.cpu() for p in ps], hs_in, w.cpu(), 1e-5, bits, 128, mode)
+        for r in range(W):
+            n = max(0, min(M, (r + 1) * R) - r * R)
+            assert torch.equal(hs[r].cpu()[:n], h_ref[r][:n]), (rep, r)
+            assert torch.equal(xs[r], xs[0]), (rep, r)
+        x0 = xs[0].cpu()
+        assert (x0 != x_ref).float().mean().item() < 0.01
+        assert spec.rel_l2(x0.float(), x_ref.float()) < (2e-3 if bits >= 8 else 2e-2)
+        hs_in = h_ref  # the second call continues from the updated shards
+
+
+def test_gemm_fused_all_reduce_norm_single_rank(cuda_device):
+    """GEMM with the scatter epilogue + norm kernel == GEMM, then the norm all-reduce."""
+    from quantized_flash_communication_b200.ops import gemm as G
+    from quantized_flash_communication_b200.parallel import QuantAllReduce
+    ar = QuantAllReduce(None, cuda_device, bits=8, group_size=128, quant_type="asym", algo="two_shot")
+    for M, K, H in [(256, 512, 1024), (1000, 1376, 4096)]:
+        a = torch.randn(M, K, device=cuda_device, dtype=torch.bfloat16)
+        wt = torch.randn(H, K, device=cuda_device, dtype=torch.bfloat16) * 0.05
+        nw = (torch.rand(H, device=cuda_device) + 0.5).to(torch.bfloat16)
+        h0 = torch.randn(M, H, device=cuda_device, dtype=torch.bfloat16)
+        h1, h2 = h0.clone(), h0.clone()
+        x1 = ar.gemm_all_reduce_norm(a, wt, h1, nw, 1e-5)
+        ar.check()
+        x2 = ar.all_reduce_norm(G.linear(a, wt), h2, nw, 1e-5)
+        ar.check()
+        assert torch.equal(h1, h2) and torch.equal(x1, x2), (M, K, H)
+
+
 def test_timeout_reports_status_and_context_survives(cuda_device):
     """Rank 0 of a 2-rank workspace whose peer never runs: every wait must expire."""
     C = ext()

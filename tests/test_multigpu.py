@@ -98,16 +98,16 @@ def _case_model(rank, world):
     out = {}
     ref = LlamaTP(cfg, TPContext(device=dev, world=1), dev, init="full", seed=9)
     _, h1 = ref.prefill(ids, return_last_hidden=True)
-    for bits in (16, 8):
-        tp = TPContext(None, dev, ar_backend="qfc", bits=bits, group_size=128)
+    for bits, sp in ((16, False), (8, False), (16, True), (8, True)):
+        tp = TPContext(None, dev, ar_backend="qfc", bits=bits, group_size=128, seq_parallel=sp)
         m = LlamaTP(cfg, tp, dev, init="full", seed=9)
         cache = m.new_cache(4, 100)
         tok, h = m.prefill(ids, cache, return_last_hidden=True)
         tok2 = m.decode_step(tok, cache)
         gathered = [torch.empty_like(h) for _ in range(world)]
         dist.all_gather(gathered, h)
-        out[bits] = dict(err=rel_l2(h.float(), h1.float()), same=all(torch.equal(g, h) for g in gathered),
-                         tok2_shape=tuple(tok2.shape))
+        out[(bits, sp)] = dict(err=rel_l2(h.float(), h1.float()), same=all(torch.equal(g, h) for g in gathered),
+                               tok2_shape=tuple(tok2.shape), sp_used=tp.sp_active(ids.numel(), cfg.hidden_size))
         tp.ar.check()
     return out
 
@@ -175,9 +175,11 @@ def test_gemm_fused_scatter_matches_oracle_on_every_rank():
 def test_tp_model_matches_tp1():
     res = _run("_case_model")
     for rank, r in res.items():
-        assert r[16]["err"] < 0.02, r
-        assert r[8]["err"] < 0.08, r
-        assert r[16]["same"] and r[8]["same"]
+        for sp in (False, True):  # plain all-reduce, and the sequence-parallel residual
+            assert r[(16, sp)]["err"] < 0.02, r
+            assert r[(8, sp)]["err"] < 0.08, r
+            assert r[(16, sp)]["same"] and r[(8, sp)]["same"]
+            assert r[(8, sp)]["sp_used"] == sp
 
 
 @need2
