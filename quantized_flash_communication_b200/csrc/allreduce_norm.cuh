@@ -108,37 +108,52 @@ __global__ void __launch_bounds__(512) two_shot_norm_kernel(const __grid_constan
       if (g >= M) continue;
       T* hrow = h + (int64_t)rr * H;
       float ss = 0.f;
-      for (int u = 0; u < upr; ++u) {
-        const int64_t loc = (int64_t)rr * H + (u << 8) + lane_off;
-        Wire8 wv[NW];
+      // NU units per batch so that NU * W slot loads (and NU residual loads) are in flight
+      constexpr int NU = (WC > 0 && kBatch / NW > 1) ? kBatch / NW : 1;
+      for (int u0 = 0; u0 < upr; u0 += NU) {
+        Wire8 wv[NU][NW];
+        float hv[NU][8];
 #pragma unroll
-        for (int s = 0; s < NW; ++s) {
-          if (s < W && !(s == rank && !p.quantize_local)) {
-            const char* slot = my + p.rs_off + (int64_t)s * p.slot1;
-            wv[s] = load_wire<P1, InT>(slot, slot + p.pay1, loc, 7, p.meta_fp32);
+        for (int a = 0; a < NU; ++a) {
+          if (u0 + a < upr) {
+            const int64_t loc = (int64_t)rr * H + ((u0 + a) << 8) + lane_off;
+#pragma unroll
+            for (int s = 0; s < NW; ++s) {
+              if (s < W && !(s == rank && !p.quantize_local)) {
+                const char* slot = my + p.rs_off + (int64_t)s * p.slot1;
+                wv[a][s] = load_wire<P1, InT>(slot, slot + p.pay1, loc, 7, p.meta_fp32);
+              }
+            }
+            Vec8IO<T>::load(hrow + ((u0 + a) << 8) + lane_off, hv[a]);
           }
         }
-        float acc[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int a = 0; a < NU; ++a) {
+          if (u0 + a < upr) {
+            const int u = u0 + a;
+            float acc[8];
 #pragma unroll
-        for (int s = 0; s < NW; ++s) {
-          if (s < W) {
-            float d[8];
-            if (s == rank && !p.quantize_local) load8_guard(in, (int64_t)g * H + (u << 8) + lane_off, (int64_t)M * H, d);
-            else decode_wire<P1, InT>(wv[s], p.meta_fp32, d);
+            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], d[i]);
+            for (int s = 0; s < NW; ++s) {
+              if (s < W) {
+                float d[8];
+                if (s == rank && !p.quantize_local)
+                  load8_guard(in, (int64_t)g * H + (u << 8) + lane_off, (int64_t)M * H, d);
+                else
+                  decode_wire<P1, InT>(wv[a][s], p.meta_fp32, d);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], d[i]);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              hv[a][i] = to_f32(from_f32<T>(to_f32(from_f32<T>(acc[i])) + hv[a][i]));
+              ss += hv[a][i] * hv[a][i];
+            }
+            Vec8IO<T>::store(hrow + (u << 8) + lane_off, hv[a]);
           }
         }
-        float hv[8];
-        Vec8IO<T>::load(hrow + (u << 8) + lane_off, hv);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          hv[i] = to_f32(from_f32<T>(to_f32(from_f32<T>(acc[i])) + hv[i]));
-          ss += hv[i] * hv[i];
-        }
-        Vec8IO<T>::store(hrow + (u << 8) + lane_off, hv);
       }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(QFC_FULL_MASK, ss, off);
