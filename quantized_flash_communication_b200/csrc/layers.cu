@@ -176,11 +176,38 @@ __global__ void argmax_kernel(const T* __restrict__ logits, float* __restrict__ 
   const T* r = logits + row * V;
   float bv = -FLT_MAX;
   int64_t bi = INT64_MAX;
-  for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = to_f32(r[i]);
-    if (v > bv || (v == bv && i < bi)) {
-      bv = v;
-      bi = i;
+  if (sizeof(T) == 2 && (V & 7) == 0 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+    // 16-byte loads, 4 in flight per thread; a thread's elements rise in index, so the
+    // strict comparison keeps the first maximum
+    const int64_t nv = V >> 3;
+    for (int64_t c0 = threadIdx.x; c0 < nv; c0 += 4 * (int64_t)blockDim.x) {
+      float v[4][8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int64_t c = c0 + k * (int64_t)blockDim.x;
+        if (c < nv) Vec8IO<T>::load(r + c * 8, v[k]);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int64_t c = c0 + k * (int64_t)blockDim.x;
+        if (c < nv) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (v[k][j] > bv) {
+              bv = v[k][j];
+              bi = c * 8 + j;
+            }
+          }
+        }
+      }
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
+      const float v = to_f32(r[i]);
+      if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+      }
     }
   }
   __shared__ float sv[32];

@@ -81,3 +81,17 @@ def test_embedding_and_argmax(cuda_device):
     logits = torch.randn(7, 32000, device=cuda_device, dtype=torch.bfloat16)
     bv, bi = L.argmax(logits, idx_offset=100)
     assert torch.equal(bi - 100, logits.float().argmax(-1))
+
+
+@pytest.mark.parametrize("V,dtype", [(128256, torch.bfloat16), (1001, torch.bfloat16), (4096, torch.float32),
+                                     (8, torch.float16)])
+def test_argmax_first_maximum(cuda_device, V, dtype):
+    logits = torch.randn(64, V, device=cuda_device).to(dtype)
+    # ties: the same maximum at two positions of every row; the first must win
+    hi = logits.float().max().item() + 1.0
+    cols = torch.randint(0, V, (64, 2), device=cuda_device).sort(-1).values
+    logits[torch.arange(64), cols[:, 0]] = hi
+    logits[torch.arange(64), cols[:, 1]] = hi
+    bv, bi = L.argmax(logits)
+    assert torch.equal(bi, cols[:, 0])
+    assert torch.equal(bv.float(), torch.full_like(bv.float(), float(torch.tensor(hi).to(dtype))))
