@@ -766,6 +766,333 @@ void check_operand(const at::Tensor& t, const char* name) {
               "gemm: ", name, " must be row-major with 16-byte aligned rows");
 }
 
+
+// ---------------------------------------------------------------------------------------
+// Small M (decode): swapped operands.  D^T[N, M] = W[N, K] . X[M, K]^T with the weight
+// rows as the MMA's M = 128 and up to 64 tokens as its N: a tile is 128 weight rows, a
+// stage is 16 KiB of weights + 8 KiB of activations (8 stages in flight), and the tiles
+// are twice as many as with 256-row weight tiles.  Each epilogue thread owns one output
+// column (TMEM lane) for every token, so a warp's stores run along an output row.  Split-K
+// as in the main kernel (fp32 partials, the last unit of a tile sums them in split order
+// into TMEM).  EPI_STORE and EPI_RESIDUAL.
+// ---------------------------------------------------------------------------------------
+namespace small {
+
+constexpr int BW = 128;       // weight rows per tile (MMA M)
+constexpr int TN = 64;        // tokens (MMA N)
+constexpr int STAGES = 8;
+constexpr int W_BYTES = BW * BK * 2;   // 16 KiB
+constexpr int X_BYTES = TN * BK * 2;   // 8 KiB
+constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
+constexpr int TMEM_COLS_S = 128;       // 2 accumulator buffers x 64 columns
+constexpr uint32_t IDESC_S = tc::idesc_f16(BW, TN, true);
+constexpr int SMEM_BYTES_S = STAGES * STAGE_BYTES + 1024 + 256;
+
+struct SArgs {
+  int M, N, K;
+  int n_tiles, splits, kb_split;
+  __nv_bfloat16* D;
+  int ldd;
+  const __nv_bfloat16* R;  // nullptr: plain store
+  int ldr;
+  float* part;             // [tiles][splits][BW][TN]
+  int* counters;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+QFC_DEV void sfail(const SArgs& a, volatile int* ab, int code) {
+  *ab = 1;
+  if (a.status) atomicCAS(a.status, 0, code);
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_small_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const SArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem;
+  uint8_t* sX = smem + STAGES * W_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sX + STAGES * X_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  __shared__ int s_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int works = args.n_tiles * args.splits;
+  const int kbs = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(tc::smem_u32(&full[s]), 1);
+      tc::mbar_init(tc::smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(tc::smem_u32(&tfull[b]), 1);
+      tc::mbar_init(tc::smem_u32(&tempty[b]), 128);
+    }
+    tc::mbar_init(tc::smem_u32(drain), 1);
+    *s_abort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::tma_prefetch_desc(&tmW);
+    tc::tma_prefetch_desc(&tmX);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tc::smem_u32(tmem_holder), TMEM_COLS_S);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      int last_issue[STAGES];
+      for (int s = 0; s < STAGES; ++s) last_issue[s] = -1;
+      bool ok = true;
+      for (int w = blockIdx.x; w < works && ok; w += gridDim.x) {
+        const int tile = w / args.splits, sp = w - tile * args.splits;
+        const int kb0 = sp * args.kb_split, kb1 = min(kbs, kb0 + args.kb_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!tc::mbar_wait(tc::smem_u32(&empty[s]), ph ^ 1, globaltimer_ns() + args.timeout_ns, s_abort)) {
+            sfail(args, s_abort, GEMM_ERR_PRODUCER | 0x10);
+            ok = false;
+            break;
+          }
+          const uint32_t fb = tc::smem_u32(&full[s]);
+          tc::mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          tc::tma_load_2d(tc::smem_u32(sW + s * W_BYTES), &tmW, fb, kb * BK, tile * BW);
+          tc::tma_load_2d(tc::smem_u32(sX + s * X_BYTES), &tmX, fb, kb * BK, 0);
+          last_issue[s] = it;
+        }
+      }
+      if (!ok || *s_abort) {
+        for (int s = 0; s < STAGES; ++s) {
+          if (last_issue[s] < 0) continue;
+          int never = 0;
+          tc::mbar_wait(tc::smem_u32(&full[s]), (last_issue[s] / STAGES) & 1, globaltimer_ns() + 50000000ull, &never);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int it = 0, t = 0;
+      bool ok = true, issued = false;
+      for (int w = blockIdx.x; w < works && ok; w += gridDim.x, ++t) {
+        const int kb0 = (w % args.splits) * args.kb_split, kb1 = min(kbs, kb0 + args.kb_split);
+        const int buf = t & 1;
+        if (!tc::mbar_wait(tc::smem_u32(&tempty[buf]), ((t >> 1) & 1) ^ 1, globaltimer_ns() + args.timeout_ns,
+                           s_abort)) {
+          sfail(args, s_abort, GEMM_ERR_MMA | 0x10);
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t tmem_d = tmem_base + (uint32_t)(buf * TN);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!tc::mbar_wait(tc::smem_u32(&full[s]), ph, globaltimer_ns() + args.timeout_ns, s_abort)) {
+            sfail(args, s_abort, GEMM_ERR_MMA | 0x11);
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t a0 = tc::smem_u32(sW + s * W_BYTES), b0 = tc::smem_u32(sX + s * X_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            tc::umma_f16(tmem_d, tc::sw128_kmajor_desc(a0 + k * 32), tc::sw128_kmajor_desc(b0 + k * 32), IDESC_S,
+                         (kb != kb0) || (k != 0));
+          issued = true;
+          tc::umma_commit(tc::smem_u32(&empty[s]));
+        }
+        if (!ok) break;
+        tc::umma_commit(tc::smem_u32(&tfull[buf]));
+      }
+      if ((!ok || *s_abort) && issued) {
+        tc::umma_commit(tc::smem_u32(drain));
+        int never = 0;
+        tc::mbar_wait(tc::smem_u32(drain), 0, globaltimer_ns() + 50000000ull, &never);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int nl = q * 32 + lane;  // weight row in the tile = TMEM lane = output column
+    int t = 0;
+    for (int w = blockIdx.x; w < works; w += gridDim.x, ++t) {
+      const int tile = w / args.splits;
+      const int buf = t & 1;
+      if (!tc::mbar_wait(tc::smem_u32(&tfull[buf]), (t >> 1) & 1, globaltimer_ns() + args.timeout_ns, s_abort)) {
+        sfail(args, s_abort, GEMM_ERR_EPI | 0x10);
+        break;
+      }
+      tc::tc_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t)(buf * TN) + ((uint32_t)(q * 32) << 16);
+      const int n = tile * BW + nl;
+      if (args.splits > 1) {
+        const int S = args.splits, sp = w - tile * S;
+        float* mine = args.part + (((int64_t)tile * S + sp) * BW + nl) * TN;
+#pragma unroll 1
+        for (int c = 0; c < TN; c += 32) {
+          uint32_t r[32];
+          tc::tmem_ld_32x32b_x32(taddr + c, r);
+          tc::tmem_wait_ld();
+          tc::tmem_reg_fence(r);
+          if (n < args.N) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              reinterpret_cast<uint4*>(mine + c)[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+          }
+        }
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) {
+          const int prev = atomicAdd(args.counters + tile, 1);
+          s_last = (prev == S - 1);
+          if (prev == S - 1) args.counters[tile] = 0;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!s_last) {
+          tc::tc_fence_before();
+          tc::mbar_arrive(tc::smem_u32(&tempty[buf]));
+          continue;
+        }
+        __threadfence();
+        const float* p0 = args.part + ((int64_t)tile * S * BW + nl) * TN;
+#pragma unroll 1
+        for (int c = 0; c < TN; c += 32) {
+          float acc[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+          if (n < args.N) {
+            for (int s2 = 0; s2 < S; ++s2) {
+              const float4* src = reinterpret_cast<const float4*>(p0 + (int64_t)s2 * BW * TN + c);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 x = __ldcg(src + j);
+                acc[4 * j] += x.x;
+                acc[4 * j + 1] += x.y;
+                acc[4 * j + 2] += x.z;
+                acc[4 * j + 3] += x.w;
+              }
+            }
+          }
+          uint32_t r[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(acc[j]);
+          tc::tmem_st_32x32b_x32(taddr + c, r);
+        }
+        tc::tmem_wait_st();
+      }
+      // epilogue: column n of D for every token m
+#pragma unroll 1
+      for (int c = 0; c < TN; c += 32) {
+        uint32_t r[32];
+        tc::tmem_ld_32x32b_x32(taddr + c, r);
+        tc::tmem_wait_ld();
+        tc::tmem_reg_fence(r);
+        if (n < args.N) {
+#pragma unroll 4
+          for (int j = 0; j < 32; ++j) {
+            const int m = c + j;
+            if (m < args.M) {
+              float v = __uint_as_float(r[j]);
+              if (args.R != nullptr) v = to_f32(from_f32<__nv_bfloat16>(v)) + to_f32(args.R[(int64_t)m * args.ldr + n]);
+              args.D[(int64_t)m * args.ldd + n] = from_f32<__nv_bfloat16>(v);
+            }
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(tc::smem_u32(&tempty[buf]));
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, TMEM_COLS_S);
+  }
+}
+
+// Swapped-operand kernel for M <= 64 unless QFC_GEMM_SMALL=0.
+bool small_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("QFC_GEMM_SMALL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+int* small_counters(int dev, int tiles) {
+  constexpr int kMaxTiles = 1 << 14;
+  static int* buf[64] = {nullptr};
+  static std::mutex mu;
+  TORCH_CHECK(tiles <= kMaxTiles, "gemm_small: too many tiles");
+  std::lock_guard<std::mutex> lock(mu);
+  if (buf[dev] == nullptr) {
+    void* p = nullptr;
+    C10_CUDA_CHECK(cudaMalloc(&p, kMaxTiles * sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(p, 0, kMaxTiles * sizeof(int)));
+    buf[dev] = static_cast<int*>(p);
+  }
+  return buf[dev];
+}
+
+// out[M, N] = a[M, K] @ b[N, K]^T (+ residual), M <= 64.
+void launch_small(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const at::Tensor* R, double timeout_ms) {
+  const int M = (int)a.size(0), K = (int)a.size(1), N = (int)b.size(0);
+  const int dev = a.get_device();
+  static bool attr_set[64] = {false};
+  if (!attr_set[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES_S));
+    attr_set[dev] = true;
+  }
+  SArgs s;
+  std::memset(&s, 0, sizeof(s));
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  s.n_tiles = (N + BW - 1) / BW;
+  const int kbs = (K + BK - 1) / BK;
+  const int sms = sm_count(dev);
+  s.splits = 1;
+  s.kb_split = kbs;
+  at::Tensor part;
+  if (s.n_tiles < sms && kbs >= 8) {
+    const int S = std::min(sms / s.n_tiles, kbs / 4);
+    if (S > 1) {
+      s.kb_split = (kbs + S - 1) / S;
+      s.splits = (kbs + s.kb_split - 1) / s.kb_split;
+      part = at::empty({(int64_t)s.n_tiles * s.splits * BW * TN},
+                       at::TensorOptions().dtype(at::kFloat).device(at::kCUDA, dev));
+      s.part = part.data_ptr<float>();
+      s.counters = small_counters(dev, s.n_tiles);
+    }
+  }
+  s.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  s.ldd = (int)out.stride(0);
+  s.R = R ? reinterpret_cast<const __nv_bfloat16*>(R->data_ptr()) : nullptr;
+  s.ldr = R ? (int)R->stride(0) : 0;
+  s.status = status_word();
+  s.timeout_ns = (uint64_t)(timeout_ms * 1e6);
+  const CUtensorMap tW = make_tmap(b.data_ptr(), N, K, b.stride(0), BW);
+  const CUtensorMap tX = make_tmap(a.data_ptr(), M, K, a.stride(0), TN);
+  const int grid = std::min(s.n_tiles * s.splits, sms);
+  gemm_small_kernel<<<grid, NUM_THREADS, SMEM_BYTES_S, at::cuda::getCurrentCUDAStream()>>>(tW, tX, s);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace small
 }  // namespace gemm
 
 // out = a @ b^T (epi 0), silu(a @ gate^T) * (a @ up^T) with b = [gate; up] (epi 1),
@@ -791,6 +1118,10 @@ at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& b, const c10::option
     TORCH_CHECK(residual.has_value(), "gemm(residual): residual tensor required");
     check_operand(*residual, "residual");
     TORCH_CHECK(residual->size(0) == M && residual->size(1) == N, "gemm: bad residual shape");
+  }
+  if (M <= small::TN && max_ctas <= 0 && (epi == EPI_STORE || epi == EPI_RESIDUAL) && small::small_enabled()) {
+    small::launch_small(a, b, out, epi == EPI_RESIDUAL ? &*residual : nullptr, timeout_ms);
+    return out;
   }
   switch (epi) {
     case EPI_STORE: launch<EPI_STORE>(a, b, &out, nullptr, M, N, K, timeout_ms, (int)max_ctas); break;
