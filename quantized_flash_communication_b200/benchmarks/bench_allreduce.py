@@ -10,6 +10,9 @@ error against the exact fp32 sum, and the fraction of the NVLink roofline: the b
 rank must push over NVLink (two-shot: 2 (W-1)/W of the quantized payload; one-shot:
 (W-1) x payload) at the measured 770 GB/s per direction, divided by the time.
 ``--reference`` also times the reference's flash_all_reduce (baseline/_ref, unmodified).
+``--norm`` also times, for two-shot points with group 128, the all-reduce followed by the
+residual add + RMSNorm on every row (the tensor-parallel layer's tail) against the
+sequence-parallel kernel that does both on the rows each rank owns.
 Rank 0 prints one JSON line per point.
 """
 from __future__ import annotations
@@ -66,6 +69,36 @@ def _wire_bytes(n, W, bits, gs, one_shot):
     return (W - 1) / W * n * (per_elem(p1) + per_elem(p2))
 
 
+def _norm_point(ar, xs, tokens, hidden, bits, rank, W, dev, iters, t_ar):
+    """all-reduce + residual RMSNorm of every row vs the sequence-parallel kernel."""
+    from ..ops import layers as L
+    eps = 1e-5
+    w = torch.ones(hidden, dtype=torch.bfloat16, device=dev)
+    h_full = torch.randn(tokens, hidden, device=dev).to(torch.bfloat16)
+    R = (tokens + W - 1) // W
+    h_shard = torch.zeros(R, hidden, dtype=torch.bfloat16, device=dev)
+    n = max(0, min(tokens, (rank + 1) * R) - rank * R)
+    h_shard[:n] = h_full[rank * R:rank * R + n]
+    out = torch.empty_like(xs)
+    x_out = torch.empty_like(xs)
+    ar.reserve_rows(tokens, hidden, (bits,))
+
+    def plain():
+        ar(xs, out=out)
+        L.rmsnorm(out, w, eps, residual=h_full, out=x_out)
+
+    def fused():
+        ar.all_reduce_norm(xs, h_shard, w, eps, out=x_out)
+
+    t_plain = _time(plain, iters)
+    t_sp = _time(fused, iters)
+    ar.check()
+    if rank == 0:
+        print(json.dumps({"impl": "allreduce_then_rmsnorm_vs_sequence_parallel", "W": W, "tokens": tokens,
+                          "hidden": hidden, "bits": bits, "allreduce_ms": t_ar, "allreduce_plus_rmsnorm_ms": t_plain,
+                          "allreduce_norm_sp_ms": t_sp, "speedup": t_plain / t_sp}), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", default="1,16,128,1024,4096,16384")
@@ -75,6 +108,7 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--algo", default="auto")
     ap.add_argument("--reference", action="store_true")
+    ap.add_argument("--norm", action="store_true")
     args = ap.parse_args(argv)
     rank, W, dev = init_distributed()
     ar_cache = {}
@@ -127,6 +161,8 @@ def main(argv=None):
                         rec["speedup_vs_reference"] = t_ref / t
                     if rank0:
                         print(json.dumps(rec), flush=True)
+                    if args.norm and gs == 128 and not one and hidden % 256 == 0:
+                        _norm_point(ar, xs, tokens, hidden, bits, rank, W, dev, args.iters, t)
     reset_communicators()
     ar_cache.clear()
     dist.destroy_process_group()
