@@ -3,11 +3,13 @@
     python -m quantized_flash_communication_b200.benchmarks.kernel_probe gemm 8192 4096 4096
     python -m quantized_flash_communication_b200.benchmarks.kernel_probe attention 8 1024 32 32
     python -m quantized_flash_communication_b200.benchmarks.kernel_probe allreduce 2 16384 4096 8
+    python -m quantized_flash_communication_b200.benchmarks.kernel_probe allreduce_norm 2 8192 4096 8
     python -m quantized_flash_communication_b200.benchmarks.kernel_probe quantize 67108864
     python -m quantized_flash_communication_b200.benchmarks.kernel_probe decode 64 4096 16 4
 
 Each subcommand runs ``--iters`` launches (default 3) after one warm-up and prints the
-median device time; ``allreduce`` runs W ranks emulated inside one launch on one GPU.
+median device time; ``allreduce`` and ``allreduce_norm`` (the sequence-parallel
+all-reduce + residual + RMSNorm) run W ranks emulated inside one launch on one GPU.
 """
 from __future__ import annotations
 
@@ -21,7 +23,7 @@ from .timing import median, time_fn
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "attention", "allreduce", "quantize", "decode"])
+    ap.add_argument("kernel", choices=["gemm", "attention", "allreduce", "allreduce_norm", "quantize", "decode"])
     ap.add_argument("shape", nargs="*", type=int)
     ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args(argv)
@@ -46,6 +48,15 @@ def main(argv=None):
         xs = [torch.randn(T, H, device=dev, dtype=torch.bfloat16) for _ in range(W)]
         outs = [torch.empty_like(x) for x in xs]
         fn, work = (lambda: ar(xs, outs)), float(W * T * H)
+    elif args.kernel == "allreduce_norm":
+        from ..parallel import EmulatedQuantAllReduce
+        W, T, H, bits = args.shape or (2, 8192, 4096, 8)
+        ar = EmulatedQuantAllReduce(W, dev, bits=bits, group_size=128, algo="two_shot")
+        R = (T + W - 1) // W
+        xs = [torch.randn(T, H, device=dev, dtype=torch.bfloat16) for _ in range(W)]
+        hs = [torch.randn(R, H, device=dev, dtype=torch.bfloat16) for _ in range(W)]
+        w = torch.ones(H, device=dev, dtype=torch.bfloat16)
+        fn, work = (lambda: ar.all_reduce_norm(xs, hs, w, 1e-5)), float(W * T * H)
     elif args.kernel == "quantize":
         from ..ops import quant as Q
         (n,) = args.shape or (1 << 26,)
