@@ -17,8 +17,11 @@ _ERR: Exception | None = None
 _COUNTING = None  # dict name -> calls while counting
 
 # Kernels launched per call of an extension function (default 1).
+# Host-only entries count 0; the fused GEMM + all-reduce entries launch the GEMM and the
+# reduce kernel; decode attention launches its partial and merge kernels.
 _KERNELS_PER_CALL = {"attn_decode": 2, "quantize_cpu": 0, "dequantize_cpu": 0, "pack_int4_cpu": 0,
-                     "unpack_int4_cpu": 0, "ar_plan": 0, "gemm_status": 0, "Workspace": 0}
+                     "unpack_int4_cpu": 0, "ar_plan": 0, "ar_plan_rows": 0, "gemm_status": 0, "attn_status": 0,
+                     "Workspace": 0, "gemm_all_reduce": 2, "gemm_all_reduce_norm": 2}
 
 
 def _load():
