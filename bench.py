@@ -41,7 +41,7 @@ def _parse():
     ap.add_argument("--group-size", type=int, default=128)
     ap.add_argument("--quant-type", default="asym")
     ap.add_argument("--ar-backend", default="qfc", choices=["qfc", "nccl", "staged"])
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=None, help="host-timed end-to-end steps (default: --steps)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch kernels eagerly instead of one CUDA graph")
     ap.add_argument("--seq-parallel", action="store_true",
@@ -119,18 +119,92 @@ def _timed(step_fn, args, dev, rank, world):
 
 
 def _timed_e2e(step_fn, args, dev):
-    """Host-timed steps that include the pinned H2D input copy and the D2H result read."""
+    """Host-timed steps that include the pinned H2D input copy and the D2H result read
+    (as many as the device-timed steps unless --e2e-steps says otherwise)."""
     import torch
-    for _ in range(1):
+    n = args.e2e_steps or args.steps
+    for _ in range(max(1, args.warmup)):
         step_fn()
     torch.cuda.synchronize()
     _barrier()
     t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
+    for _ in range(n):
         step_fn()
     t1 = time.perf_counter()
     _barrier()
-    return _max_over_ranks((t1 - t0) * 1000.0 / args.e2e_steps, dev)
+    return _max_over_ranks((t1 - t0) * 1000.0 / n, dev)
+
+
+def _peaks():
+    """Roofline denominators: the driver-measured peaks if present, else the pool's fallback."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops_sustained"]), float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1400.0, 6650.0, "fallback"
+
+
+LINK_GBS = 770.0  # measured peer copy bandwidth per direction on this pool's B200s
+
+
+def _step_flops(cfg, B, S):
+    """FLOPs of one prefill step of the whole model: the linear layers over every token,
+    causal attention, and the lm_head over the last token of each sequence."""
+    H, hd = cfg.hidden_size, cfg.head_dim
+    qkv = H * (cfg.num_heads + 2 * cfg.num_kv_heads) * hd
+    per_layer = 2 * B * S * (qkv + cfg.num_heads * hd * H + 3 * H * cfg.intermediate_size)
+    per_layer += 2 * B * cfg.num_heads * S * S * hd  # QK^T and PV, causal half of each
+    return cfg.num_layers * per_layer + 2 * B * H * cfg.vocab_size
+
+
+def _wire_bytes_per_step(cfg, B, S, W, bits, gs):
+    """Bytes one rank pushes over NVLink per step: two two-shot all-reduces per layer of
+    [B*S, H], each 2 (W-1)/W of the quantized payload plus fp16 (scale, zero) per group."""
+    if W == 1:
+        return 0.0
+    from quantized_flash_communication_b200.quantization import phase_bits
+    p1, p2 = phase_bits(bits)
+
+    def per_elem(p):
+        return 2.0 if p == 16 else p / 8.0 + 4.0 / gs
+    n = B * S * cfg.hidden_size
+    return cfg.num_layers * 2 * (W - 1) / W * n * (per_elem(p1) + per_elem(p2))
+
+
+def _quant_error(model, tp, ids, dev):
+    """Relative L2 error of one step's all-reduce against the exact fp32 sum.
+
+    Runs layer 0 of a real step up to o_proj on this rank, forms its partial sum, and
+    all-reduces it twice: through the model's quantized path and exactly in fp32 (NCCL,
+    outside any timed region).  The fused GEMM epilogue is bit-identical to this unfused
+    pair, so the error is that of the step's all-reduces."""
+    import torch
+    import torch.distributed as dist
+    from quantized_flash_communication_b200.ops import attention as A
+    from quantized_flash_communication_b200.ops import gemm as G
+    from quantized_flash_communication_b200.ops import layers as L
+    from quantized_flash_communication_b200.quantization import rel_l2
+    if tp.world == 1 or tp.ar is None:
+        return None
+    cfg = model.cfg
+    B, S = ids.shape
+    lay = model.model.layers[0]
+    h = L.embedding(ids.reshape(-1), model.model.embed_tokens.weight)
+    x = L.rmsnorm(h, lay.input_layernorm.weight, cfg.rms_eps)
+    qkv = G.linear(x, lay.self_attn.qkv_fused)
+    pos = torch.arange(S, device=dev, dtype=torch.int64).repeat(B)
+    L.rope_kv(qkv, pos, model.cos_sin, model.nq, model.nkv, model.hd, None, None, None)
+    o = A.prefill_attention(qkv, B, S, model.nq, model.nkv, model.hd)
+    p = G.linear(o, lay.self_attn.o_proj.weight)
+    exact = p.float()
+    dist.all_reduce(exact)
+    got = tp.all_reduce(p.clone())
+    torch.cuda.synchronize()
+    err = torch.tensor([rel_l2(got.float(), exact)], device=dev, dtype=torch.float64)
+    dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    return float(err.item())
 
 
 # ------------------------------------------------------------------------------------------
@@ -208,6 +282,7 @@ def run_ours(args):
     if tp.ar is not None:
         tp.ar.check()
     assert gemm_status() == 0, "a GEMM kernel reported a pipeline timeout"
+    qerr = _quant_error(model, tp, ids, dev) if args.ar_backend == "qfc" else None
 
     e2e = None
     if not args.no_e2e:
@@ -229,6 +304,15 @@ def run_ours(args):
                "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
                "api": "LlamaTP.capture_prefill (CUDA graph)" if graphed is not None else "LlamaTP.prefill"}
     weights_gb = sum(p.numel() * p.element_size() for p in model.parameters()) / 1e9
+    peak_tf, _, peak_src = _peaks()
+    flops = _step_flops(cfg, B, S)
+    wire = _wire_bytes_per_step(cfg, B, S, world, args.bits, args.group_size) if args.ar_backend == "qfc" else 0.0
+    t_compute = flops / world / (peak_tf * 1e12) * 1e3
+    t_link = wire / (LINK_GBS * 1e9) * 1e3
+    roofline = {"fraction": max(t_compute, t_link) / ms, "compute_ms_at_peak": t_compute,
+                "nvlink_ms_at_770gbs": t_link, "flops_per_step": flops, "nvlink_bytes_per_rank": wire,
+                "peak_tflops": peak_tf, "peaks": f"{peak_src} (bf16 sustained)",
+                "note": "the slower of compute at peak and bytes over NVLink, divided by the step time"}
     res = {
         "metric": "tp_prefill_throughput_llama2_7b",
         "value": B * S / (ms / 1000.0),
@@ -250,11 +334,14 @@ def run_ours(args):
                                  + (", sequence-parallel residual + RMSNorm in the all-reduce"
                                     if tp.sp_active(B * S, cfg.hidden_size) else "")
                                  if args.ar_backend == "qfc" else args.ar_backend) if world > 1 else "none (tp1)",
-                   "attention": A.prefill_backend(),
+                   "attention": A.prefill_backend(cfg.head_dim),
                    "launch": "cuda_graph" if graphed is not None else "eager",
                    "l2": f"no flush; each step streams {weights_gb:.1f} GB of weights per rank (> 126 MB L2)"},
         "clocks": clocks,
         "e2e": e2e,
+        "roofline_fraction": roofline["fraction"],
+        "roofline": roofline,
+        "quant_rel_l2": qerr,
         "gpu_launches": launches_per_step * args.steps,
         "gpu_launches_per_step": launches_per_step,
         "impl": "ours",

@@ -3,6 +3,8 @@
 // (attn_decode_noalloc.cu).
 #pragma once
 
+#include <atomic>
+
 #include <cfloat>
 #include <type_traits>
 
@@ -525,21 +527,32 @@ decode_partial_mma_kernel(const T* __restrict__ q, const T* __restrict__ kc, con
   }
 }
 
-template <typename T, int HD, int G>
-inline cudaError_t decode_mma_prepare() {
-  static const cudaError_t err = cudaFuncSetAttribute(decode_partial_mma_kernel<T, HD, G>,
-                                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                      decode_mma_smem_bytes<HD>());
+// Opts a kernel into more than 48 KB of dynamic shared memory on the CURRENT device.
+// The attribute belongs to one device's context, so the opt-in is tracked per device
+// (one bit per device in `done`); a process that launches on several GPUs sets it on each.
+template <typename Kern>
+inline cudaError_t opt_in_smem_per_device(Kern kern, int bytes, std::atomic<unsigned long long>& done) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  const unsigned long long bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
   return err;
 }
 
-// Opts the partial kernel into its dynamic shared memory (once per instantiation).
+template <typename T, int HD, int G>
+inline cudaError_t decode_mma_prepare() {
+  static std::atomic<unsigned long long> done{0};
+  return opt_in_smem_per_device(decode_partial_mma_kernel<T, HD, G>, decode_mma_smem_bytes<HD>(), done);
+}
+
+// Opts the partial kernel into its dynamic shared memory (once per instantiation and device).
 template <typename T, int HD, int G>
 inline cudaError_t decode_prepare() {
-  static const cudaError_t err = cudaFuncSetAttribute(decode_partial_kernel<T, HD, G>,
-                                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                      decode_smem_bytes<HD>());
-  return err;
+  static std::atomic<unsigned long long> done{0};
+  return opt_in_smem_per_device(decode_partial_kernel<T, HD, G>, decode_smem_bytes<HD>(), done);
 }
 
 // Pass 2.  One warp per (sequence, query head): lane p reads partition p's (max, sum),

@@ -21,21 +21,28 @@ static __device__ __align__(256) float qfc_noalloc_scratch[QFC_NOALLOC_SCRATCH_B
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-float* g_scratch[kMaxDevices] = {nullptr};
+float* g_scratch[kMaxDevices] = {nullptr};  // guarded by g_mu
+int g_sms[kMaxDevices] = {0};               // guarded by g_mu
 
-// Device address of the scratch array on the current device, looked up once per device.
-// In host code the array's name is only a host-side stand-in; passing it to a kernel
-// would be wrong, so the address always comes from cudaGetSymbolAddress.
-int scratch_for_current_device(float** out) {
+// Device address of the scratch array on the current device and that device's SM count,
+// both looked up once per device under g_mu.  In host code the array's name is only a
+// host-side stand-in; passing it to a kernel would be wrong, so the address always comes
+// from cudaGetSymbolAddress.
+int scratch_for_current_device(float** out, int* sms) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QFC_NOALLOC_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_mu);
   if (g_scratch[dev] == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, qfc_noalloc_scratch) != cudaSuccess || p == nullptr) return QFC_NOALLOC_ERR_CUDA;
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      return QFC_NOALLOC_ERR_CUDA;
+    g_sms[dev] = n;
     g_scratch[dev] = static_cast<float*>(p);
   }
   *out = g_scratch[dev];
+  *sms = g_sms[dev];
   return QFC_NOALLOC_OK;
 }
 
@@ -44,25 +51,13 @@ unsigned long long needed_bytes(int batch, int nq, int hd, int page, int max_pag
   return (unsigned long long)batch * nq * parts * (hd + 2) * sizeof(float);
 }
 
-int sm_count() {
-  static int sms[kMaxDevices] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
-  if (sms[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    sms[dev] = n;
-  }
-  return sms[dev];
-}
-
 template <typename T, int HD, int G>
 int launch(const void* q, const void* kc, const void* vc, const int* bt, const int* sl, void* out, int B, int nq,
-           int nkv, int page, int max_pages, float scale, float* scratch, cudaStream_t st) {
+           int nkv, int page, int max_pages, float scale, float* scratch, int sms, cudaStream_t st) {
   const int page_shift = ilog2_exact(page);
   if (page_shift < 0) return QFC_NOALLOC_ERR_BAD_ARGS;
   const int max_ctx = max_pages * page;
-  const int part_tok = decode_part_tokens(B, nkv, max_ctx, sm_count());
+  const int part_tok = decode_part_tokens(B, nkv, max_ctx, sms);
   const int n_parts = (max_ctx + part_tok - 1) / part_tok;
   float* part_o = scratch;
   float* part_ml = scratch + (size_t)B * nq * n_parts * HD;
@@ -75,8 +70,9 @@ int launch(const void* q, const void* kc, const void* vc, const int* bt, const i
 
 template <typename T>
 int dispatch(int hd, int G, const void* q, const void* kc, const void* vc, const int* bt, const int* sl, void* out,
-             int B, int nq, int nkv, int page, int max_pages, float scale, float* scratch, cudaStream_t st) {
-#define QFC_NA(HD_, G_) return launch<T, HD_, G_>(q, kc, vc, bt, sl, out, B, nq, nkv, page, max_pages, scale, scratch, st)
+             int B, int nq, int nkv, int page, int max_pages, float scale, float* scratch, int sms, cudaStream_t st) {
+#define QFC_NA(HD_, G_) \
+  return launch<T, HD_, G_>(q, kc, vc, bt, sl, out, B, nq, nkv, page, max_pages, scale, scratch, sms, st)
   if (hd == 128) {
     switch (G) {
       case 1: QFC_NA(128, 1);
@@ -114,15 +110,16 @@ int qfc_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_ca
   if (needed_bytes(batch, num_q_heads, head_dim, page_size, max_pages_per_seq) > QFC_NOALLOC_SCRATCH_BYTES)
     return QFC_NOALLOC_ERR_TOO_LARGE;
   float* scratch = nullptr;
-  const int rc = scratch_for_current_device(&scratch);
+  int sms = 0;
+  const int rc = scratch_for_current_device(&scratch, &sms);
   if (rc != QFC_NOALLOC_OK) return rc;
   const int G = num_q_heads / num_kv_heads;
   if (dtype == 0)
     return dispatch<__nv_bfloat16>(head_dim, G, q, k_cache, v_cache, block_table, seq_lens, out, batch, num_q_heads,
-                                   num_kv_heads, page_size, max_pages_per_seq, scale, scratch, stream);
+                                   num_kv_heads, page_size, max_pages_per_seq, scale, scratch, sms, stream);
   if (dtype == 1)
     return dispatch<__half>(head_dim, G, q, k_cache, v_cache, block_table, seq_lens, out, batch, num_q_heads,
-                            num_kv_heads, page_size, max_pages_per_seq, scale, scratch, stream);
+                            num_kv_heads, page_size, max_pages_per_seq, scale, scratch, sms, stream);
   return QFC_NOALLOC_ERR_BAD_ARGS;
 }
 

@@ -50,7 +50,9 @@ void rope_kv_cuda(at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& cos_
                   const c10::optional<at::Tensor>& slot_mapping, int64_t nq, int64_t nkv, int64_t hd);
 void silu_mul_cuda(const at::Tensor& gu, at::Tensor& out);
 void embedding_cuda(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t vocab_start);
-void argmax_cuda(const at::Tensor& logits, at::Tensor& best_val, at::Tensor& best_idx, int64_t idx_offset);
+void argmax_cuda(const at::Tensor& logits, at::Tensor& best_val, at::Tensor& best_idx, int64_t idx_offset,
+                 int64_t valid, const c10::optional<at::Tensor>& rng, double inv_temp,
+                 const c10::optional<at::Tensor>& done);
 // attn_decode.cu
 void attn_decode_cuda(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& bt,
                       const at::Tensor& sl, at::Tensor& out, int64_t nq, int64_t nkv, int64_t hd, double scale);
@@ -103,7 +105,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v_cache"), py::arg("slot_mapping"), py::arg("nq"), py::arg("nkv"), py::arg("hd"));
   m.def("silu_mul", &qfc::silu_mul_cuda);
   m.def("embedding", &qfc::embedding_cuda);
-  m.def("argmax", &qfc::argmax_cuda);
+  m.def("argmax", &qfc::argmax_cuda, py::arg("logits"), py::arg("best_val"), py::arg("best_idx"),
+        py::arg("idx_offset") = 0, py::arg("valid") = -1, py::arg("rng") = py::none(), py::arg("inv_temp") = 1.0,
+        py::arg("done") = py::none());
   m.def("attn_decode", &qfc::attn_decode_cuda, "paged split-KV decode attention");
   m.def("attn_prefill", &qfc::attn_prefill_cuda, "causal flash prefill attention (tcgen05)");
   m.def("attn_status", &qfc::attn_status, py::arg("clear") = false);

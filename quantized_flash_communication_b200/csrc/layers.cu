@@ -168,18 +168,52 @@ __global__ void embedding_kernel(const int64_t* __restrict__ ids, const T* __res
   }
 }
 
-// Row-wise (max value, argmax) over logits [M, V] (first index wins ties).
-template <typename T>
+// Counter-based random bits for sampling: the SplitMix64 output function (Steele, Lea and
+// Flood, "Fast splittable pseudorandom number generators", OOPSLA 2014) applied to a key
+// built from (seed, step, row, vocabulary index).  The same key gives the same bits on
+// every rank and at every tensor-parallel degree, so ranks that sample their own slice of
+// the vocabulary agree on the token without exchanging random state.
+QFC_DEV uint64_t mix64(uint64_t z) {
+  z += 0x9e3779b97f4a7c15ull;
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+
+// Standard Gumbel noise -log(-log(u)) with u in (0, 1) from 24 random bits.
+QFC_DEV float gumbel_noise(uint64_t seed, uint64_t step, int64_t row, int64_t idx) {
+  const uint64_t h = mix64(mix64(mix64(seed ^ (step * 0xd1b54a32d192ed03ull)) ^ (uint64_t)row) ^ (uint64_t)idx);
+  const float u = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+  return -logf(-logf(u));
+}
+
+// Row-wise (max score, argmax) over logits [M, V] (row stride V; only the first V_valid
+// columns count; the first index wins ties).  Greedy: score = logit.  SAMPLE: score =
+// logit * inv_temp + Gumbel noise keyed by (rng[0] = seed, rng[1] = step, row, global
+// index), whose argmax is an exact draw from softmax(logit * inv_temp) (the Gumbel-max
+// trick); the last CTA to finish then advances rng[1], so a captured decode step samples
+// afresh on every replay.
+template <typename T, bool SAMPLE>
 __global__ void argmax_kernel(const T* __restrict__ logits, float* __restrict__ best_val, int64_t* __restrict__ best_idx,
-                              int64_t V, int64_t idx_offset) {
+                              int64_t V, int64_t V_valid, int64_t idx_offset, int64_t* __restrict__ rng,
+                              float inv_temp, unsigned int* __restrict__ done) {
   const int64_t row = blockIdx.x;
   const T* r = logits + row * V;
   float bv = -FLT_MAX;
   int64_t bi = INT64_MAX;
+  uint64_t seed = 0, step = 0;
+  if constexpr (SAMPLE) {
+    seed = (uint64_t)rng[0];
+    step = (uint64_t)rng[1];
+  }
+  auto score = [&](float v, int64_t i) -> float {
+    if constexpr (SAMPLE) return v * inv_temp + gumbel_noise(seed, step, row, i + idx_offset);
+    else return v;
+  };
   if (sizeof(T) == 2 && (V & 7) == 0 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
     // 16-byte loads, 4 in flight per thread; a thread's elements rise in index, so the
     // strict comparison keeps the first maximum
-    const int64_t nv = V >> 3;
+    const int64_t nv = (V_valid + 7) >> 3;
     for (int64_t c0 = threadIdx.x; c0 < nv; c0 += 4 * (int64_t)blockDim.x) {
       float v[4][8];
 #pragma unroll
@@ -193,17 +227,21 @@ __global__ void argmax_kernel(const T* __restrict__ logits, float* __restrict__ 
         if (c < nv) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            if (v[k][j] > bv) {
-              bv = v[k][j];
-              bi = c * 8 + j;
+            const int64_t i = c * 8 + j;
+            if (i < V_valid) {
+              const float sc = score(v[k][j], i);
+              if (sc > bv) {
+                bv = sc;
+                bi = i;
+              }
             }
           }
         }
       }
     }
   } else {
-    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
-      const float v = to_f32(r[i]);
+    for (int64_t i = threadIdx.x; i < V_valid; i += blockDim.x) {
+      const float v = score(to_f32(r[i]), i);
       if (v > bv || (v == bv && i < bi)) {
         bv = v;
         bi = i;
@@ -242,7 +280,16 @@ __global__ void argmax_kernel(const T* __restrict__ logits, float* __restrict__ 
     }
     if (lane == 0) {
       best_val[row] = bv;
-      best_idx[row] = bi + idx_offset;
+      best_idx[row] = (bi == INT64_MAX) ? -1 : bi + idx_offset;
+      if constexpr (SAMPLE) {
+        // every CTA read rng[1] before it arrives here; the last arrival advances it
+        __threadfence();
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+          rng[1] = (int64_t)(step + 1);
+          *done = 0u;
+          __threadfence();
+        }
+      }
     }
   }
 }
@@ -368,16 +415,33 @@ void embedding_cuda(const at::Tensor& ids, const at::Tensor& table, at::Tensor& 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void argmax_cuda(const at::Tensor& logits, at::Tensor& best_val, at::Tensor& best_idx, int64_t idx_offset) {
+void argmax_cuda(const at::Tensor& logits, at::Tensor& best_val, at::Tensor& best_idx, int64_t idx_offset,
+                 int64_t valid, const c10::optional<at::Tensor>& rng, double inv_temp,
+                 const c10::optional<at::Tensor>& done) {
   TORCH_CHECK(logits.is_contiguous() && logits.dim() == 2, "argmax: contiguous [M, V] logits");
   const int64_t M = logits.size(0), V = logits.size(1);
+  const int64_t V_valid = valid < 0 ? V : std::min<int64_t>(valid, V);
   if (M == 0) return;
+  const bool sample = rng.has_value();
+  if (sample) {
+    TORCH_CHECK(rng->scalar_type() == at::kLong && rng->numel() >= 2 && rng->is_cuda(),
+                "argmax: rng must be an int64 CUDA tensor [seed, step]");
+    TORCH_CHECK(done.has_value() && done->scalar_type() == at::kInt && done->is_cuda(),
+                "argmax: sampling needs an int32 CUDA arrival counter (zero before the first call)");
+  }
   c10::cuda::CUDAGuard guard(logits.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  int64_t* rp = sample ? rng->data_ptr<int64_t>() : nullptr;
+  unsigned int* dp = sample ? reinterpret_cast<unsigned int*>(done->data_ptr<int>()) : nullptr;
   auto launch = [&](auto tag) {
     using T = decltype(tag);
-    argmax_kernel<T><<<M, 1024, 0, st>>>(reinterpret_cast<const T*>(logits.data_ptr()), best_val.data_ptr<float>(),
-                                         best_idx.data_ptr<int64_t>(), V, idx_offset);
+    const T* lp = reinterpret_cast<const T*>(logits.data_ptr());
+    if (sample)
+      argmax_kernel<T, true><<<M, 1024, 0, st>>>(lp, best_val.data_ptr<float>(), best_idx.data_ptr<int64_t>(), V,
+                                                 V_valid, idx_offset, rp, (float)inv_temp, dp);
+    else
+      argmax_kernel<T, false><<<M, 1024, 0, st>>>(lp, best_val.data_ptr<float>(), best_idx.data_ptr<int64_t>(), V,
+                                                  V_valid, idx_offset, nullptr, 1.f, nullptr);
   };
   if (logits.scalar_type() == at::kBFloat16) launch(__nv_bfloat16());
   else if (logits.scalar_type() == at::kHalf) launch(__half());

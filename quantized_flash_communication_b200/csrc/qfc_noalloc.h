@@ -14,7 +14,9 @@
  * bytes of it and returns QFC_NOALLOC_ERR_TOO_LARGE (doing nothing) above that.
  *
  * The first call on each device looks up the array's device address (with that device
- * current).  Make that first call before any CUDA stream capture begins.
+ * current) and opts the kernels into their shared memory on that device.  Make that first
+ * call before any CUDA stream capture begins.  One process may call it on several GPUs:
+ * each device has its own copy of the array, address and opt-in.
  *
  * All calls share the one array and it keeps the last call's contents; every value a
  * call reads from it was written earlier in the same call, so nothing needs clearing.

@@ -32,8 +32,9 @@ from ..ops import layers as L
 from ..parallel.quant_allreduce import QuantAllReduce
 from ..utils.trace import maybe_region
 from .config import LlamaConfig, get_config
+from .sampling import Sampler
 
-__all__ = ["TPContext", "LlamaTP", "KVCache", "smoke_forward"]
+__all__ = ["TPContext", "LlamaTP", "KVCache", "Sampler", "smoke_forward"]
 
 
 # ------------------------------------------------------------------------------------------
@@ -156,6 +157,15 @@ class TPContext:
             p = G.linear(x, w)
         with maybe_region(self.timer, "  (allreduce part)"):
             return self.all_reduce(p, out=p)
+
+    def gather_vocab(self, logits: torch.Tensor) -> torch.Tensor:
+        """Full-vocabulary logits [B, W * V_local] from every rank's vocabulary slice."""
+        if self.world == 1:
+            return logits
+        B, V = logits.shape
+        buf = torch.empty(self.world, B, V, dtype=logits.dtype, device=logits.device)
+        dist.all_gather_into_tensor(buf, logits.contiguous(), group=self.group)
+        return buf.permute(1, 0, 2).reshape(B, self.world * V)
 
     def gather_argmax(self, val: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
         """Global argmax from per-rank (max value, index) pairs; ties go to the lower index."""
@@ -483,9 +493,17 @@ class LlamaTP(nn.Module):
         with maybe_region(t, "rmsnorm"):
             return L.rmsnorm(ar, nxt, eps, residual=h)
 
-    def _head(self, x_last: torch.Tensor) -> torch.Tensor:
+    def _head(self, x_last: torch.Tensor, sampler: Optional[Sampler] = None) -> torch.Tensor:
+        """Next token per row: greedy, or drawn by ``sampler`` (the same on every rank)."""
         logits = G.linear(x_last, self.lm_head.weight)
-        val, idx = L.argmax(logits, self.vocab_start)
+        valid = max(0, min(self.v_local, self.cfg.vocab_size - self.vocab_start))  # padded rows never count
+        if sampler is not None and sampler.top_p < 1.0:
+            full = self.tp.gather_vocab(logits)[:, : self.cfg.vocab_size]
+            return sampler.full(full)
+        if sampler is not None:
+            val, idx = sampler.local(logits, self.vocab_start, valid)
+        else:
+            val, idx = L.argmax(logits, self.vocab_start, valid=valid)
         return self.tp.gather_argmax(val, idx)
 
     @torch.no_grad()
@@ -540,22 +558,25 @@ class LlamaTP(nn.Module):
         return x
 
     @torch.no_grad()
-    def prefill(self, ids: torch.Tensor, cache: Optional[KVCache] = None, return_last_hidden: bool = False):
-        """Causal forward over ``ids [B, S]`` (int64, on device); returns greedy next tokens [B].
+    def prefill(self, ids: torch.Tensor, cache: Optional[KVCache] = None, return_last_hidden: bool = False,
+                sampler: Optional[Sampler] = None):
+        """Causal forward over ``ids [B, S]`` (int64, on device); returns the next tokens [B]
+        (greedy, or drawn by ``sampler``).
 
         With ``cache``, k/v of all positions are written to it and ``seq_lens`` becomes S.
         """
         B, S = ids.shape
         x = self._hidden(ids, cache)
         x_last = x.view(B, S, -1)[:, -1].contiguous()
-        nxt = self._head(x_last)
+        nxt = self._head(x_last, sampler)
         if return_last_hidden:
             return nxt, x_last
         return nxt
 
     @torch.no_grad()
-    def decode_step(self, tokens: torch.Tensor, cache: KVCache) -> torch.Tensor:
-        """One token per sequence: appends to the cache and returns greedy next tokens [B]."""
+    def decode_step(self, tokens: torch.Tensor, cache: KVCache, sampler: Optional[Sampler] = None) -> torch.Tensor:
+        """One token per sequence: appends to the cache and returns the next tokens [B]
+        (greedy, or drawn by ``sampler``)."""
         B = tokens.numel()
         cfg = self.cfg
         t = self.timer
@@ -577,7 +598,7 @@ class LlamaTP(nn.Module):
         for li in range(cfg.num_layers):
             x = self._layer(li, h, x, attn, pos, slots, cache)
         with maybe_region(t, "lm_head+argmax"):
-            return self._head(x)
+            return self._head(x, sampler)
 
     @torch.no_grad()
     def capture_prefill(self, batch: int, seq: int, cache: Optional[KVCache] = None,
@@ -603,11 +624,13 @@ class LlamaTP(nn.Module):
         return GraphedStep(graph, ids, out)
 
     @torch.no_grad()
-    def capture_decode(self, cache: KVCache, warmup: int = 2) -> "GraphedStep":
+    def capture_decode(self, cache: KVCache, warmup: int = 2, sampler: Optional[Sampler] = None) -> "GraphedStep":
         """Capture one decode step (one token per sequence) as a CUDA graph.
 
         The graph reads positions from ``cache.seq_lens`` on the device, so the same graph
-        serves every step; the caller must not exceed the cache's capacity.
+        serves every step; the caller must not exceed the cache's capacity.  With
+        ``sampler`` the step samples; its step counter lives on the device, so every replay
+        draws fresh noise (the warm-up steps advance it too).
         """
         B = cache.seq_lens.numel()
         tok = torch.zeros(B, dtype=torch.int64, device=self.device)
@@ -616,29 +639,40 @@ class LlamaTP(nn.Module):
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side):
             for _ in range(warmup):
-                self.decode_step(tok, cache)
+                self.decode_step(tok, cache, sampler)
                 cache.seq_lens.copy_(saved)
         torch.cuda.current_stream(self.device).wait_stream(side)
         torch.cuda.synchronize(self.device)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            out = self.decode_step(tok, cache)
+            out = self.decode_step(tok, cache, sampler)
         cache.seq_lens.copy_(saved)  # capture does not run the kernels, but keep state explicit
         return GraphedStep(graph, tok, out)
 
     @torch.no_grad()
-    def generate(self, ids: torch.Tensor, max_new_tokens: int, cache: Optional[KVCache] = None) -> torch.Tensor:
-        """Greedy generation; returns [B, max_new_tokens] new tokens."""
+    def generate(self, ids: torch.Tensor, max_new_tokens: int, cache: Optional[KVCache] = None,
+                 do_sample: bool = False, temperature: float = 1.0, top_p: float = 1.0,
+                 seed: Optional[int] = None, sampler: Optional[Sampler] = None) -> torch.Tensor:
+        """Generate ``max_new_tokens`` tokens per sequence; returns them as [B, max_new_tokens].
+
+        Greedy by default.  ``do_sample=True`` samples from softmax(logits / temperature),
+        restricted to the top-p nucleus when ``top_p < 1`` (the knobs of Hugging Face
+        ``generate``, which the reference calls with ``do_sample=True, temperature=0.7``).
+        Every rank draws the same tokens: the seed is rank 0's (``seed`` or a random one),
+        broadcast once.  Collective: all ranks of the group call it together.
+        """
+        if sampler is None and do_sample:
+            sampler = Sampler(self.tp, temperature=temperature, top_p=top_p, seed=seed)
         B, S = ids.shape
         if cache is None:
             cache = self.new_cache(B, S + max_new_tokens)
         if S + max_new_tokens - 1 > cache.capacity:
             raise ValueError(f"cache holds {cache.capacity} tokens per sequence; {S} + {max_new_tokens} requested")
         out = torch.empty(B, max_new_tokens, dtype=torch.int64, device=self.device)
-        tok = self.prefill(ids, cache)
+        tok = self.prefill(ids, cache, sampler=sampler)
         out[:, 0] = tok
         for t in range(1, max_new_tokens):
-            tok = self.decode_step(tok, cache)
+            tok = self.decode_step(tok, cache, sampler)
             out[:, t] = tok
         return out
 

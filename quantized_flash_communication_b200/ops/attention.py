@@ -1,13 +1,13 @@
 """Attention operators: causal prefill over the fused qkv activation, paged decode.
 
-``prefill_attention`` runs the tcgen05 flash kernel of ``csrc/attn_prefill.cu`` for bf16
-with head_dim 128 (every Llama configuration here); other head sizes fall back to torch's
-SDPA.  ``decode_attention`` runs the paged split-KV kernel of ``csrc/attn_decode.cu``.
+``prefill_attention`` runs the tcgen05 flash kernel of ``csrc/attn_prefill.cu``: bf16 on a
+CUDA device with head_dim 128 (every Llama configuration here).  Any other input raises
+instead of silently running a library kernel.  ``decode_attention`` runs the paged
+split-KV kernel of ``csrc/attn_decode.cu``.
 """
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from .._ext import ext
 
@@ -19,25 +19,21 @@ def _native(qkv: torch.Tensor, hd: int) -> bool:
 
 
 def prefill_backend(hd: int = 128) -> str:
-    return "qfc-tcgen05" if hd == 128 else "sdpa"
+    """Name of the kernel that serves prefill attention for head size ``hd``."""
+    if hd != 128:
+        raise ValueError(f"prefill attention has a kernel for head_dim 128 only, not {hd}")
+    return "qfc-tcgen05"
 
 
 def prefill_attention(qkv: torch.Tensor, B: int, S: int, nq: int, nkv: int, hd: int,
                       out: torch.Tensor | None = None) -> torch.Tensor:
     """Causal self-attention of B sequences of length S; qkv [B*S, (nq+2nkv)*hd] -> [B*S, nq*hd]."""
-    if _native(qkv, hd):
-        o = torch.empty(B * S, nq * hd, dtype=qkv.dtype, device=qkv.device) if out is None else out
-        ext().attn_prefill(qkv, o, B, S, nq, nkv, hd, 1.0 / hd ** 0.5)
-        return o
-    x = qkv.view(B, S, nq + 2 * nkv, hd)
-    q = x[:, :, :nq].transpose(1, 2)
-    k = x[:, :, nq:nq + nkv].transpose(1, 2)
-    v = x[:, :, nq + nkv:].transpose(1, 2)
-    o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=(nq != nkv))
-    o = o.transpose(1, 2).reshape(B * S, nq * hd)
-    if out is not None:
-        out.copy_(o)
-        return out
+    if not _native(qkv, hd):
+        raise NotImplementedError(
+            f"prefill_attention: the tcgen05 kernel takes bf16 CUDA tensors with head_dim 128; got "
+            f"{qkv.dtype} on {qkv.device} with head_dim {hd}")
+    o = torch.empty(B * S, nq * hd, dtype=qkv.dtype, device=qkv.device) if out is None else out
+    ext().attn_prefill(qkv, o, B, S, nq, nkv, hd, 1.0 / hd ** 0.5)
     return o
 
 

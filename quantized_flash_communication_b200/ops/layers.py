@@ -58,10 +58,17 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, vocab_start: int = 0,
     return y
 
 
-def argmax(logits: torch.Tensor, idx_offset: int = 0):
-    """Row-wise (max value fp32, argmax int64 + idx_offset) of ``logits [M, V]``."""
+def argmax(logits: torch.Tensor, idx_offset: int = 0, valid: Optional[int] = None,
+           rng: Optional[torch.Tensor] = None, inv_temp: float = 1.0, done: Optional[torch.Tensor] = None):
+    """Row-wise (max score fp32, argmax int64 + idx_offset) of ``logits [M, V]``.
+
+    Only the first ``valid`` columns take part (all by default).  With ``rng`` (int64
+    [seed, step] on the device) the score is ``logit * inv_temp`` plus Gumbel noise, so the
+    argmax is a sample from softmax(logit * inv_temp); the kernel then advances the step
+    (``done``: an int32 arrival counter on the device, zero before the first call).
+    """
     M = logits.shape[0]
     bv = torch.empty(M, dtype=torch.float32, device=logits.device)
     bi = torch.empty(M, dtype=torch.int64, device=logits.device)
-    ext().argmax(logits, bv, bi, idx_offset)
+    ext().argmax(logits, bv, bi, idx_offset, -1 if valid is None else int(valid), rng, float(inv_temp), done)
     return bv, bi

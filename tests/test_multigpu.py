@@ -112,6 +112,24 @@ def _case_model(rank, world):
     return out
 
 
+def _case_sampling(rank, world):
+    """Every rank must draw the same sampled tokens (temperature and top-p paths)."""
+    from quantized_flash_communication_b200.models.config import get_config
+    from quantized_flash_communication_b200.models.llama import LlamaTP, TPContext
+    dev = torch.device("cuda", rank)
+    cfg = get_config("tiny-mha")
+    ids = torch.randint(0, cfg.vocab_size, (3, 20), generator=torch.Generator().manual_seed(8)).to(dev)
+    m = LlamaTP(cfg, TPContext(None, dev, ar_backend="qfc", bits=8), dev, init="full", seed=4)
+    out = {}
+    for top_p in (1.0, 0.9):
+        toks = m.generate(ids, 10, do_sample=True, temperature=0.7, top_p=top_p)  # seed from rank 0
+        gathered = [torch.empty_like(toks) for _ in range(world)]
+        dist.all_gather(gathered, toks)
+        out[top_p] = all(torch.equal(g, toks) for g in gathered)
+    m.tp.ar.check()
+    return out
+
+
 def _case_peer_never_joins(rank, world):
     """Rank 1 skips an all-reduce: rank 0's kernel must time out and report it."""
     from quantized_flash_communication_b200.parallel import CommTimeoutError, QuantAllReduce
@@ -180,6 +198,13 @@ def test_tp_model_matches_tp1():
             assert r[(8, sp)]["err"] < 0.08, r
             assert r[(16, sp)]["same"] and r[(8, sp)]["same"]
             assert r[(8, sp)]["sp_used"] == sp
+
+
+@need2
+def test_sampled_generation_is_identical_on_every_rank():
+    res = _run("_case_sampling")
+    for rank, r in res.items():
+        assert r[1.0] and r[0.9], (rank, r)
 
 
 @need2
