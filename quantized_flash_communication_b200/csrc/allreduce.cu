@@ -1,6 +1,8 @@
 // Host side of the fused quantized all-reduce: planning, argument checks, dispatch.
 // The kernels are in allreduce.cuh and are instantiated per input dtype in
 // allreduce_inst_*.cu (compiled in parallel).
+#include <cfloat>
+
 #include "allreduce.cuh"
 #include "scatter.h"
 
@@ -177,6 +179,101 @@ void gemm_all_reduce(const WsPtr& ws, const at::Tensor& a, const at::Tensor& w, 
   prm.sym = sym ? 1 : 0;
   prm.quantize_local = 1;
   dispatch_gemm_reduce<__nv_bfloat16, __nv_bfloat16>(prm, pl, pl.chunk >> 8, dev, at::cuda::getCurrentCUDAStream());
+}
+
+
+// ---------------------------------------------------------------------------------------
+// Cross-rank argmax of a vocabulary-parallel head (one kernel)
+// ---------------------------------------------------------------------------------------
+// Every rank holds, per row, the (score, global index) of its best vocabulary entry
+// (greedy logit or sampled Gumbel score).  Thread t pushes row t's pair into every peer's
+// argmax slot, the CTA publishes one flag per peer, waits (bounded) for the W - 1 peers'
+// flags and writes the winner: the highest score, ties to the lower rank, i.e. to the
+// lower vocabulary index.  Slots are double-buffered by epoch parity: a rank can only
+// start call k + 1 after every peer has started call k, so no peer is still reading the
+// buffer it writes.  Replaces the reference's full-vocabulary head on every rank
+// (Hugging Face lm_head in main.py:190-194) with one small exchange.
+namespace {
+__global__ void __launch_bounds__(512) argmax_gather_kernel(const __grid_constant__ ARParams p, const float* val,
+                                                            const int64_t* idx, int64_t* out, int rows,
+                                                            int64_t argmax_off) {
+  const int rank = p.rank, W = p.world;
+  const int t = threadIdx.x;
+  char* my = p.base[rank];
+  uint32_t* ep = p.epochs[rank] + ALG_ARGMAX * kMaxBlocks;
+  __shared__ uint32_t s_e;
+  __shared__ int s_abort;
+  if (t == 0) {
+    s_e = *ep + 1u;
+    s_abort = 0;
+  }
+  __syncthreads();
+  const uint32_t e = s_e;
+  const int64_t region = argmax_off + (int64_t)(e & 1u) * (kArgmaxBytes / 2);
+  float v = -FLT_MAX;
+  int32_t ix = -1;
+  if (t < rows) {
+    v = val[t];
+    ix = (int32_t)idx[t];
+    const uint2 pair = make_uint2(__float_as_uint(v), (uint32_t)ix);
+    for (int j = 0; j < W; ++j) {
+      if (j == rank) continue;
+      *reinterpret_cast<uint2*>(p.base[j] + region + ((int64_t)rank * kArgmaxRows + t) * 8) = pair;
+    }
+  }
+  __syncthreads();
+  if (t < W && t != rank) st_release_sys(flag_at(p.base[t], PH_ARGMAX, 0, rank), e);
+  if (!wait_sources(p, my, PH_ARGMAX, 0, rank, W, e, true, &s_abort)) return;
+  if (t < rows) {
+    float best = -FLT_MAX;
+    int32_t bi = -1;
+    for (int r = 0; r < W; ++r) {  // rank order = vocabulary order: the first maximum wins
+      float rv;
+      int32_t ri;
+      if (r == rank) {
+        rv = v;
+        ri = ix;
+      } else {
+        const uint2 pr = __ldcg(reinterpret_cast<const uint2*>(my + region + ((int64_t)r * kArgmaxRows + t) * 8));
+        rv = __uint_as_float(pr.x);
+        ri = (int32_t)pr.y;
+      }
+      if (ri >= 0 && (bi < 0 || rv > best)) {
+        best = rv;
+        bi = ri;
+      }
+    }
+    out[t] = bi;
+  }
+  if (t == 0) *ep = e;
+}
+}  // namespace
+
+// out[t] = the global argmax of row t over every rank's (val[t], idx[t]).  rows <= 512.
+void argmax_gather(const WsPtr& ws, const at::Tensor& val, const at::Tensor& idx, at::Tensor& out,
+                   double timeout_ms) {
+  TORCH_CHECK(ws->peers_ready(), "argmax_gather: workspace peers not mapped");
+  TORCH_CHECK(val.is_cuda() && val.scalar_type() == at::kFloat && val.is_contiguous(), "argmax_gather: fp32 val");
+  TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous() && out.scalar_type() == at::kLong &&
+                  out.is_contiguous(), "argmax_gather: int64 idx / out");
+  const int64_t rows = val.numel();
+  TORCH_CHECK(idx.numel() == rows && out.numel() == rows, "argmax_gather: size mismatch");
+  TORCH_CHECK(rows <= kArgmaxRows, "argmax_gather: at most ", kArgmaxRows, " rows");
+  if (rows == 0) return;
+  c10::cuda::CUDAGuard guard(val.device());
+  ARParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  const int W = (int)ws->world();
+  for (int r = 0; r < W; ++r) prm.base[r] = ws->peer_base(r);
+  prm.rank = (int)ws->rank();
+  prm.world = W;
+  prm.epochs[prm.rank] = ws->epochs();
+  prm.status = ws->status_dev();
+  prm.timeout_ns = (uint64_t)(timeout_ms * 1e6);
+  const int threads = std::max(32, (int)((rows + 31) / 32 * 32));
+  argmax_gather_kernel<<<1, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      prm, val.data_ptr<float>(), idx.data_ptr<int64_t>(), out.data_ptr<int64_t>(), (int)rows, ws->argmax_off());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace qfc

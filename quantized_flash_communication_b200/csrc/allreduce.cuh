@@ -7,7 +7,7 @@
 // asymmetric or symmetric groups.  The reference runs it as ~7W+10 kernel launches, six
 // NCCL collectives and two host synchronisations per call; here it is a single launch:
 //
-//   phase 1  every CTA quantizes its 256-element units of every chunk in registers and
+//   phase 1  every CTA quantizes its warp units of every chunk in registers and
 //            stores the packed codes + per-group metadata straight into the chunk owner's
 //            reduce-scatter slot (plain st.global to the peer's mapped buffer), then
 //            publishes a per-(block, source) flag with a release store;
@@ -49,7 +49,7 @@ struct ARParams {
   KernelStatus* status;
   uint32_t* gemm_epoch;  // FROM_GEMM: this rank's fused-GEMM epoch counter (device)
   int64_t n;       // elements
-  int64_t chunk;   // two-shot: elements per chunk; one-shot: n rounded up to 256
+  int64_t chunk;   // two-shot: elements per chunk (a multiple of 512); one-shot: n rounded up to 256
   int64_t rs_off, ag_off, os_off, os_bytes;
   int64_t slot1, slot2;  // slot strides in bytes (one-shot uses slot1)
   int64_t pay1, pay2;    // payload bytes at the head of a slot; metadata follows
@@ -539,6 +539,484 @@ __global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ A
 }
 
 // ---------------------------------------------------------------------------------------
+// Two-shot kernel with 16 elements per lane (16-bit inputs, group sizes 16..256)
+// ---------------------------------------------------------------------------------------
+// The same protocol, slot layout and arithmetic as two_shot_kernel, restructured for
+// throughput: a warp unit is 512 elements (16 per lane), so an INT8 lane stores its codes
+// as one 16-byte vector, the per-lane address / guard / group-parameter work is spread
+// over twice the elements, and the metadata of a unit's groups leaves as whole 16-byte
+// vectors gathered by shuffles instead of one 4-byte store per group.  The (-min, max)
+// statistics of a lane's 16 values are reduced on packed 16-bit pairs before the
+// cross-lane levels.  Results are bit-identical to two_shot_kernel.
+constexpr int kEPL = 16;
+constexpr int kUnit16 = 32 * kEPL;  // elements per warp unit
+constexpr int kWarps16 = 8;         // warps per CTA: 256 threads, three CTAs per SM (80 registers)
+
+// 16 consecutive 16-bit elements as two 16-byte vectors; elements at or beyond n read 0.
+struct Raw16 {
+  uint4 a, b;
+};
+template <typename T>
+QFC_DEV Raw16 load_raw16(const T* base, int64_t idx, int64_t n) {
+  Raw16 r;
+  if (idx + kEPL <= n) {
+    const uint4* p = reinterpret_cast<const uint4*>(base + idx);
+    r.a = p[0];
+    r.b = p[1];
+  } else {
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(base);
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t lo = (idx + 2 * i < n) ? h[idx + 2 * i] : 0u;
+      const uint32_t hi = (idx + 2 * i + 1 < n) ? h[idx + 2 * i + 1] : 0u;
+      w[i] = lo | (hi << 16);
+    }
+    r.a = make_uint4(w[0], w[1], w[2], w[3]);
+    r.b = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+  return r;
+}
+template <typename T>
+QFC_DEV void raw16_to_f32(const Raw16& r, float (&v)[16]) {
+  const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) unpack_bf16x2(w[i], v[2 * i], v[2 * i + 1]);
+    else unpack_f16x2(w[i], v[2 * i], v[2 * i + 1]);
+  }
+}
+template <typename T>
+QFC_DEV void store16_guard(T* base, int64_t idx, int64_t n, const float (&v)[16]) {
+  if (idx + kEPL <= n) {
+    uint4* d = reinterpret_cast<uint4*>(base + idx);
+    const float(&lo)[8] = *reinterpret_cast<const float(*)[8]>(&v[0]);
+    const float(&hi)[8] = *reinterpret_cast<const float(*)[8]>(&v[8]);
+    d[0] = Vec8IO<T>::pack(lo);
+    d[1] = Vec8IO<T>::pack(hi);
+  } else {
+#pragma unroll
+    for (int i = 0; i < kEPL; ++i)
+      if (idx + i < n) base[idx + i] = from_f32<T>(v[i]);
+  }
+}
+
+// Group (min, max) of 16-bit inputs: the lane's 16 values reduce as packed pairs, then
+// the (-min, max) pair crosses lpg lanes as one word per shuffle level.  Exact.
+template <typename T>
+QFC_DEV void group_minmax16x16(const Raw16& r, int lpg, float& mn, float& mx) {
+  using T2 = typename std::conditional<std::is_same<T, __nv_bfloat16>::value, __nv_bfloat162, __half2>::type;
+  auto as2 = [](uint32_t u) { return *reinterpret_cast<T2*>(&u); };
+  auto bits = [](T2 x) { return *reinterpret_cast<uint32_t*>(&x); };
+  const T2 hi = __hmax2(__hmax2(__hmax2(as2(r.a.x), as2(r.a.y)), __hmax2(as2(r.a.z), as2(r.a.w))),
+                        __hmax2(__hmax2(as2(r.b.x), as2(r.b.y)), __hmax2(as2(r.b.z), as2(r.b.w))));
+  const T2 lo = __hmin2(__hmin2(__hmin2(as2(r.a.x), as2(r.a.y)), __hmin2(as2(r.a.z), as2(r.a.w))),
+                        __hmin2(__hmin2(as2(r.b.x), as2(r.b.y)), __hmin2(as2(r.b.z), as2(r.b.w))));
+  const uint32_t nlo = bits(lo) ^ 0x80008000u;             // (-min_even, -min_odd)
+  const uint32_t q1 = __byte_perm(nlo, bits(hi), 0x7610);  // (-min_even, max_odd)
+  const uint32_t q2 = __byte_perm(nlo, bits(hi), 0x5432);  // (-min_odd,  max_even)
+  uint32_t p = bits(__hmax2(as2(q1), as2(q2)));            // (-min, max)
+  for (int off = lpg >> 1; off > 0; off >>= 1) p = bits(__hmax2(as2(p), as2(__shfl_xor_sync(QFC_FULL_MASK, p, off))));
+  float a, b;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) unpack_bf16x2(p, a, b);
+  else unpack_f16x2(p, a, b);
+  mn = -a;
+  mx = b;
+}
+// Same for fp32 values (the reduced sum in phase 2).
+QFC_DEV void group_minmax_f32x16(const float (&v)[16], int lpg, float& mn, float& mx) {
+  float a[4], b[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    a[q] = fminf(fminf(v[q], v[q + 4]), fminf(v[q + 8], v[q + 12]));
+    b[q] = fmaxf(fmaxf(v[q], v[q + 4]), fmaxf(v[q + 8], v[q + 12]));
+  }
+  mn = fminf(fminf(a[0], a[1]), fminf(a[2], a[3]));
+  mx = fmaxf(fmaxf(b[0], b[1]), fmaxf(b[2], b[3]));
+  for (int off = lpg >> 1; off > 0; off >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(QFC_FULL_MASK, mn, off));
+    mx = fmaxf(mx, __shfl_xor_sync(QFC_FULL_MASK, mx, off));
+  }
+}
+
+// A lane's 16 values in wire form: payload (P = 8: one uint4 of codes; P = 4: uint2 in .a.x,
+// .a.y; P = 16: the raw 16-bit values in .a, .b) and its group's metadata words
+// (fp16 pair in m0, or fp32 scale / zero in m0 / m1).
+struct Enc16 {
+  uint4 a, b;
+  uint32_t m0, m1;
+  float s, z;  // the scale as used for decoding (fp16-rounded unless fp32 metadata)
+};
+
+template <int P>
+QFC_DEV Enc16 encode16_stats(const float (&v)[16], float mn, float mx, bool sym, int meta_fp32) {
+  Enc16 e;
+  e.b = make_uint4(0, 0, 0, 0);
+  float s, inv, z;
+  if (sym) QMath<P, true>::params(mn, mx, s, inv, z);
+  else QMath<P, false>::params(mn, mx, s, inv, z);
+  uint32_t m[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m[i] = QMath<P, false>::codebits(v[i], inv, z);
+  const uint32_t(&m_lo)[8] = *reinterpret_cast<const uint32_t(*)[8]>(&m[0]);
+  const uint32_t(&m_hi)[8] = *reinterpret_cast<const uint32_t(*)[8]>(&m[8]);
+  if constexpr (P == 8) {
+    const uint2 u0 = codebits8_to_u2(m_lo), u1 = codebits8_to_u2(m_hi);
+    e.a = make_uint4(u0.x, u0.y, u1.x, u1.y);
+  } else {
+    e.a = make_uint4(codebits8_to_int4(m_lo), codebits8_to_int4(m_hi), 0, 0);
+  }
+  if (meta_fp32) {
+    e.m0 = __float_as_uint(s);
+    e.m1 = __float_as_uint(z);
+    e.s = s;
+  } else {
+    e.m0 = pack_f16x2(s, z);
+    e.m1 = 0;
+    e.s = __half2float(__float2half_rn(s));
+  }
+  e.z = z;
+  return e;
+}
+
+// Payload of a lane's 16 elements into a slot (codes at slot + loc * P / 8).
+template <int P>
+QFC_DEV void store_payload16(char* slot, int64_t loc, const Enc16& e) {
+  if constexpr (P == 16) {
+    uint4* d = reinterpret_cast<uint4*>(slot + loc * 2);
+    d[0] = e.a;
+    d[1] = e.b;
+  } else if constexpr (P == 8) {
+    *reinterpret_cast<uint4*>(slot + loc) = e.a;
+  } else {
+    *reinterpret_cast<uint2*>(slot + (loc >> 1)) = make_uint2(e.a.x, e.a.y);
+  }
+}
+
+// Metadata of the unit's groups as 16-byte vectors: lane v gathers groups 4v..4v+3
+// (fp16 pairs) or 2v..2v+1 (fp32 pairs) from their lanes and stores them.  gs = 256
+// (two groups per unit, fp16) stores one 8-byte vector.
+QFC_DEV void store_meta16(char* meta, int64_t unit, const Enc16& e, int lane, int gs_shift, int meta_fp32) {
+  const int lpg = 1 << (gs_shift - 4);                 // lanes per group
+  const int gpu = kUnit16 >> gs_shift;                 // groups per unit
+  const int64_t g0 = unit * gpu;                       // the unit's first group
+  if (!meta_fp32) {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = __shfl_sync(QFC_FULL_MASK, e.m0, ((lane * 4 + j) * lpg) & 31);
+    if (gpu >= 4) {
+      if (lane < (gpu >> 2)) *reinterpret_cast<uint4*>(meta + (g0 + 4 * lane) * 4) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else if (lane == 0) {
+      *reinterpret_cast<uint2*>(meta + g0 * 4) = make_uint2(w[0], w[1]);
+    }
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      w[2 * j] = __shfl_sync(QFC_FULL_MASK, e.m0, ((lane * 2 + j) * lpg) & 31);
+      w[2 * j + 1] = __shfl_sync(QFC_FULL_MASK, e.m1, ((lane * 2 + j) * lpg) & 31);
+    }
+    if (lane < (gpu >> 1)) *reinterpret_cast<uint4*>(meta + (g0 + 2 * lane) * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// A lane's 16 elements as read from a slot (local memory written by peers: L2, no L1).
+struct Wire16 {
+  uint4 a, b;
+  uint32_t m0, m1;
+};
+template <int P>
+QFC_DEV Wire16 load_wire16(const char* slot, const char* meta, int64_t loc, int gs_shift, int meta_fp32) {
+  Wire16 w;
+  w.b = make_uint4(0, 0, 0, 0);
+  w.m0 = w.m1 = 0;
+  if constexpr (P == 16) {
+    const uint4* p = reinterpret_cast<const uint4*>(slot + loc * 2);
+    w.a = __ldcg(p);
+    w.b = __ldcg(p + 1);
+  } else {
+    const int64_t g = loc >> gs_shift;
+    if (meta_fp32) {
+      const uint2 m = __ldcg(reinterpret_cast<const uint2*>(meta + g * 8));
+      w.m0 = m.x;
+      w.m1 = m.y;
+    } else {
+      w.m0 = __ldcg(reinterpret_cast<const unsigned int*>(meta + g * 4));
+    }
+    if constexpr (P == 8) {
+      w.a = __ldcg(reinterpret_cast<const uint4*>(slot + loc));
+    } else {
+      const uint2 u = __ldcg(reinterpret_cast<const uint2*>(slot + (loc >> 1)));
+      w.a = make_uint4(u.x, u.y, 0, 0);
+    }
+  }
+  return w;
+}
+template <int P, typename T>
+QFC_DEV void decode_wire16(const Wire16& w, int meta_fp32, float (&d)[16]) {
+  if constexpr (P == 16) {
+    Raw16 r;
+    r.a = w.a;
+    r.b = w.b;
+    raw16_to_f32<T>(r, d);
+  } else {
+    float s, z;
+    if (meta_fp32) {
+      s = __uint_as_float(w.m0);
+      z = __uint_as_float(w.m1);
+    } else {
+      unpack_f16x2(w.m0, s, z);
+    }
+    float(&lo)[8] = *reinterpret_cast<float(*)[8]>(&d[0]);
+    float(&hi)[8] = *reinterpret_cast<float(*)[8]>(&d[8]);
+    if constexpr (P == 8) {
+      dq_u2(make_uint2(w.a.x, w.a.y), z, s, lo);
+      dq_u2(make_uint2(w.a.z, w.a.w), z, s, hi);
+    } else {
+      dq_u2(int4_to_u2(w.a.x), z, s, lo);
+      dq_u2(int4_to_u2(w.a.y), z, s, hi);
+    }
+  }
+}
+// Values a receiver reconstructs from an Enc16 (the own chunk's output).
+template <int P, typename T>
+QFC_DEV void decode_enc16(const Enc16& e, float (&d)[16]) {
+  if constexpr (P == 16) {
+    Raw16 r;
+    r.a = e.a;
+    r.b = e.b;
+    raw16_to_f32<T>(r, d);
+  } else {
+    float(&lo)[8] = *reinterpret_cast<float(*)[8]>(&d[0]);
+    float(&hi)[8] = *reinterpret_cast<float(*)[8]>(&d[8]);
+    if constexpr (P == 8) {
+      dq_u2(make_uint2(e.a.x, e.a.y), e.z, e.s, lo);
+      dq_u2(make_uint2(e.a.z, e.a.w), e.z, e.s, hi);
+    } else {
+      dq_u2(int4_to_u2(e.a.x), e.z, e.s, lo);
+      dq_u2(int4_to_u2(e.a.y), e.z, e.s, hi);
+    }
+  }
+}
+// Wire form of a lane's 16 raw 16-bit inputs.
+template <int P, typename T>
+QFC_DEV Enc16 encode_raw16(const Raw16& r, int lpg, bool sym, int meta_fp32) {
+  if constexpr (P == 16) {
+    Enc16 e;
+    e.a = r.a;
+    e.b = r.b;
+    e.m0 = e.m1 = 0;
+    e.s = 1.f;
+    e.z = 0.f;
+    return e;
+  } else {
+    float mn, mx;
+    group_minmax16x16<T>(r, lpg, mn, mx);
+    float v[16];
+    raw16_to_f32<T>(r, v);
+    return encode16_stats<P>(v, mn, mx, sym, meta_fp32);
+  }
+}
+// Wire form of 16 fp32 values (the reduced sum); P = 16 rounds to the input type T.
+template <int P, typename T>
+QFC_DEV Enc16 encode_f32x16(const float (&v)[16], int lpg, bool sym, int meta_fp32) {
+  if constexpr (P == 16) {
+    Enc16 e;
+    const float(&lo)[8] = *reinterpret_cast<const float(*)[8]>(&v[0]);
+    const float(&hi)[8] = *reinterpret_cast<const float(*)[8]>(&v[8]);
+    e.a = Vec8IO<T>::pack(lo);
+    e.b = Vec8IO<T>::pack(hi);
+    e.m0 = e.m1 = 0;
+    e.s = 1.f;
+    e.z = 0.f;
+    return e;
+  } else {
+    float mn, mx;
+    group_minmax_f32x16(v, lpg, mn, mx);
+    return encode16_stats<P>(v, mn, mx, sym, meta_fp32);
+  }
+}
+
+// Two-shot all-reduce, 16 elements per lane.  InT: bf16 / fp16.  Group size 16..256.
+template <typename InT, typename OutT, int P1, int P2, int WC, bool FROM_GEMM = false>
+__global__ void __launch_bounds__(kWarps16 * 32, 3) two_shot16_kernel(const __grid_constant__ ARParams p) {
+  static_assert(sizeof(InT) == 2, "two_shot16_kernel takes 16-bit inputs");
+  const int rank = gridDim.y > 1 ? (int)blockIdx.y : p.rank;
+  const int W = WC > 0 ? WC : p.world;
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+  const int lpg = p.gs >> 4;
+  const InT* in = static_cast<const InT*>(p.in[rank]);
+  OutT* out = static_cast<OutT*>(p.out[rank]);
+  char* my = p.base[rank];
+  uint32_t* ep = p.epochs[rank] + ALG_TWO_SHOT * kMaxBlocks + b;
+  __shared__ uint32_t s_e;
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) {
+    s_e = *ep + 1u;
+    s_abort = 0;
+  }
+  __syncthreads();
+  const uint32_t e = s_e;
+  const int64_t C = p.chunk;
+  const int64_t units = C / kUnit16;
+  const int64_t ustride = (int64_t)gridDim.x * wpb;
+  const int64_t u0 = (int64_t)b * wpb + warp;
+  const int64_t my_units = (u0 < units) ? (units - 1 - u0) / ustride + 1 : 0;
+  const int64_t lane_off = lane * kEPL;
+
+  // Phase 1: quantize this warp's units of every chunk and push them to the chunk owners.
+  if constexpr (FROM_GEMM) {
+    const uint32_t eg = *p.gemm_epoch;  // advanced by this rank's GEMM, which ran before
+    if (!wait_sources(p, my, PH_GEMM, 0, rank, W, eg, false, &s_abort)) return;
+  } else {
+    constexpr int KB = 4;
+    const int64_t items = my_units * W;
+    for (int64_t it = 0; it < items; it += KB) {
+      Raw16 raw[KB];
+#pragma unroll
+      for (int k = 0; k < KB; ++k) {
+        if (it + k < items) {
+          int64_t i;
+          int jj;
+          split_item<WC>(it + k, W, i, jj);
+          const int j = (rank + 1 + jj) % W;  // peers staggered, own chunk last
+          raw[k] = load_raw16(in, (int64_t)j * C + (u0 + i * ustride) * kUnit16 + lane_off, p.n);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < KB; ++k) {
+        if (it + k < items) {
+          int64_t i;
+          int jj;
+          split_item<WC>(it + k, W, i, jj);
+          const int j = (rank + 1 + jj) % W;
+          if (j == rank && !p.quantize_local) continue;
+          const int64_t unit = u0 + i * ustride;
+          const Enc16 en = encode_raw16<P1, InT>(raw[k], lpg, p.sym, p.meta_fp32);
+          char* slot = p.base[j] + p.rs_off + (int64_t)rank * p.slot1;
+          store_payload16<P1>(slot, unit * kUnit16 + lane_off, en);
+          if constexpr (P1 != 16) store_meta16(slot + p.pay1, unit, en, lane, p.gs_shift, p.meta_fp32);
+        }
+      }
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < W) st_release_sys(flag_at(p.base[threadIdx.x], PH_RS, b, rank), e);
+    if (!wait_sources(p, my, PH_RS, b, rank, W, e, false, &s_abort)) return;
+  }
+
+  // Phase 2: reduce the own chunk's units, requantize, push to every peer, write own output.
+  // Sources are summed in rank order (as the oracle does), SB slot loads in flight at a
+  // time, so that a warp's registers stay within the 3-CTA-per-SM budget at W = 8.
+  {
+    constexpr int NW = WC > 0 ? WC : kMaxRanks;
+    constexpr int SBMAX = P1 == 16 ? 2 : 4;  // 16-bit payloads hold twice the registers
+    constexpr int SB = NW < SBMAX ? NW : SBMAX;
+    constexpr int NU = 1;
+    for (int64_t i0 = 0; i0 < my_units; i0 += NU) {
+      float acc[NU][16];
+#pragma unroll
+      for (int a = 0; a < NU; ++a)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[a][i] = 0.f;
+#pragma unroll
+      for (int s0 = 0; s0 < NW; s0 += SB) {
+        Wire16 wv[NU][SB];
+#pragma unroll
+        for (int a = 0; a < NU; ++a) {
+          if (i0 + a < my_units) {
+            const int64_t loc = (u0 + (i0 + a) * ustride) * kUnit16 + lane_off;
+#pragma unroll
+            for (int t = 0; t < SB; ++t) {
+              const int s = s0 + t;
+              if (s < W && !(s == rank && !p.quantize_local)) {
+                const char* slot = my + p.rs_off + (int64_t)s * p.slot1;
+                wv[a][t] = load_wire16<P1>(slot, slot + p.pay1, loc, p.gs_shift, p.meta_fp32);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int a = 0; a < NU; ++a) {
+          if (i0 + a < my_units) {
+            const int64_t loc = (u0 + (i0 + a) * ustride) * kUnit16 + lane_off;
+#pragma unroll
+            for (int t = 0; t < SB; ++t) {
+              const int s = s0 + t;
+              if (s < W) {
+                float d[16];
+                if (s == rank && !p.quantize_local) raw16_to_f32<InT>(load_raw16(in, (int64_t)rank * C + loc, p.n), d);
+                else decode_wire16<P1, InT>(wv[a][t], p.meta_fp32, d);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) acc[a][i] = __fadd_rn(acc[a][i], d[i]);
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int a = 0; a < NU; ++a) {
+        if (i0 + a < my_units) {
+          const int64_t unit = u0 + (i0 + a) * ustride;
+          const int64_t loc = unit * kUnit16 + lane_off;
+          const Enc16 en = encode_f32x16<P2, InT>(acc[a], lpg, p.sym, p.meta_fp32);
+#pragma unroll
+          for (int jj = 1; jj < NW; ++jj) {
+            if (jj < W) {
+              const int j = (rank + jj) % W;
+              char* slot = p.base[j] + p.ag_off + (int64_t)rank * p.slot2;
+              store_payload16<P2>(slot, loc, en);
+              if constexpr (P2 != 16) store_meta16(slot + p.pay2, unit, en, lane, p.gs_shift, p.meta_fp32);
+            }
+          }
+          float o[16];
+          decode_enc16<P2, InT>(en, o);
+          store16_guard(out, (int64_t)rank * C + loc, p.n, o);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < W && (int)threadIdx.x != rank) st_release_sys(flag_at(p.base[threadIdx.x], PH_AG, b, rank), e);
+  if (!wait_sources(p, my, PH_AG, b, rank, W, e, true, &s_abort)) return;
+
+  // Phase 3: dequantize the gathered chunks of the other ranks.  Items (unit, peer).
+  if (W > 1) {
+    constexpr int KB = 4;
+    const int64_t items = my_units * (W - 1);
+    for (int64_t it = 0; it < items; it += KB) {
+      Wire16 wv[KB];
+#pragma unroll
+      for (int k = 0; k < KB; ++k) {
+        if (it + k < items) {
+          int64_t i;
+          int jj;
+          split_item<(WC > 1 ? WC - 1 : 0)>(it + k, W - 1, i, jj);
+          const int j = (rank + 1 + jj) % W;
+          const int64_t loc = (u0 + i * ustride) * kUnit16 + lane_off;
+          const char* slot = my + p.ag_off + (int64_t)j * p.slot2;
+          wv[k] = load_wire16<P2>(slot, slot + p.pay2, loc, p.gs_shift, p.meta_fp32);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < KB; ++k) {
+        if (it + k < items) {
+          int64_t i;
+          int jj;
+          split_item<(WC > 1 ? WC - 1 : 0)>(it + k, W - 1, i, jj);
+          const int j = (rank + 1 + jj) % W;
+          const int64_t loc = (u0 + i * ustride) * kUnit16 + lane_off;
+          float d[16];
+          decode_wire16<P2, InT>(wv[k], p.meta_fp32, d);
+          store16_guard(out, (int64_t)j * C + loc, p.n, d);
+        }
+      }
+    }
+  }
+  if (threadIdx.x == 0) *ep = e;
+}
+
+// ---------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------
 struct Plan {
@@ -581,7 +1059,8 @@ inline Plan make_plan(int64_t n, int W, int bits, int gs, bool fp32, int in_elem
     pl.need_rs = pl.need_ag = 0;
     pl.need_os = (int64_t)W * pl.slot1;
   } else {
-    pl.chunk = align_up((std::max<int64_t>(n, 1) + W - 1) / W, 256);
+    // 512: a whole warp unit of the 16-element-per-lane kernel (and two of the 8-element one)
+    pl.chunk = align_up((std::max<int64_t>(n, 1) + W - 1) / W, 512);
     pl.pay1 = align_up(payload_bytes(pl.chunk, pl.p1, in_elem), 256);
     pl.slot1 = pl.pay1 + align_up(meta_bytes(pl.chunk, pl.p1, gs, fp32), 256);
     pl.pay2 = align_up(payload_bytes(pl.chunk, pl.p2, in_elem), 256);
@@ -602,16 +1081,21 @@ inline int num_sms(int dev) {
   return v;
 }
 
+// max_wpb: warps per CTA the kernel was compiled for (its __launch_bounds__); with
+// max_wpb < 16 the kernel is built for several CTAs per SM and the grid may use them all,
+// otherwise the grid stays at one CTA per SM.
 template <typename Kern>
-void launch_ar(Kern kern, const ARParams& prm, int64_t units, int W_emul, int dev, cudaStream_t st) {
+void launch_ar(Kern kern, const ARParams& prm, int64_t units, int W_emul, int dev, cudaStream_t st,
+               int max_wpb = 16) {
   const int sms = num_sms(dev);
-  int wpb = (int)std::min<int64_t>(16, std::max<int64_t>(2, (units + sms - 1) / sms));
+  int wpb = (int)std::min<int64_t>(max_wpb, std::max<int64_t>(2, (units + sms - 1) / sms));
   const int threads = wpb * 32;
   int occ = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, 0);
   if (occ < 1) occ = 1;
+  // every CTA must be resident at once (CTA b waits for CTA b of the other ranks)
   int64_t cap = (int64_t)occ * sms / std::max(1, W_emul);
-  cap = std::min<int64_t>(cap, std::min<int64_t>(sms, kMaxBlocks));
+  cap = std::min<int64_t>(cap, max_wpb < 16 ? (int64_t)kMaxBlocks : std::min<int64_t>(sms, kMaxBlocks));
   TORCH_CHECK(cap >= 1, "quant_all_reduce: no co-resident CTA budget (emulated world too large)");
   const int64_t G = std::max<int64_t>(1, std::min<int64_t>((units + wpb - 1) / wpb, cap));
   dim3 grid((unsigned)G, (unsigned)std::max(1, W_emul));
@@ -630,6 +1114,16 @@ void dispatch_bits_w(const ARParams& prm, const Plan& pl, bool one_shot, int64_t
     }
     return;
   }
+  if constexpr (sizeof(InT) == 2) {
+    if (prm.gs >= 16) {  // 16 elements per lane: 512-element units
+      const int64_t u16 = prm.chunk / kUnit16;
+      if (pl.p1 == 16) launch_ar(two_shot16_kernel<InT, OutT, 16, 16, WC>, prm, u16, W_emul, dev, st, kWarps16);
+      else if (pl.p1 == 8) launch_ar(two_shot16_kernel<InT, OutT, 8, 8, WC>, prm, u16, W_emul, dev, st, kWarps16);
+      else if (pl.p2 == 8) launch_ar(two_shot16_kernel<InT, OutT, 4, 8, WC>, prm, u16, W_emul, dev, st, kWarps16);
+      else launch_ar(two_shot16_kernel<InT, OutT, 4, 4, WC>, prm, u16, W_emul, dev, st, kWarps16);
+      return;
+    }
+  }
   if (pl.p1 == 16) launch_ar(two_shot_kernel<InT, OutT, 16, 16, WC>, prm, units, W_emul, dev, st);
   else if (pl.p1 == 8) launch_ar(two_shot_kernel<InT, OutT, 8, 8, WC>, prm, units, W_emul, dev, st);
   else if (pl.p2 == 8) launch_ar(two_shot_kernel<InT, OutT, 4, 8, WC>, prm, units, W_emul, dev, st);
@@ -638,10 +1132,12 @@ void dispatch_bits_w(const ARParams& prm, const Plan& pl, bool one_shot, int64_t
 
 template <typename InT, typename OutT, int WC>
 void dispatch_gemm_reduce_w(const ARParams& prm, const Plan& pl, int64_t units, int dev, cudaStream_t st) {
-  if (pl.p1 == 16) launch_ar(two_shot_kernel<InT, OutT, 16, 16, WC, true>, prm, units, 1, dev, st);
-  else if (pl.p1 == 8) launch_ar(two_shot_kernel<InT, OutT, 8, 8, WC, true>, prm, units, 1, dev, st);
-  else if (pl.p2 == 8) launch_ar(two_shot_kernel<InT, OutT, 4, 8, WC, true>, prm, units, 1, dev, st);
-  else launch_ar(two_shot_kernel<InT, OutT, 4, 4, WC, true>, prm, units, 1, dev, st);
+  (void)units;
+  const int64_t u16 = prm.chunk / kUnit16;
+  if (pl.p1 == 16) launch_ar(two_shot16_kernel<InT, OutT, 16, 16, WC, true>, prm, u16, 1, dev, st, kWarps16);
+  else if (pl.p1 == 8) launch_ar(two_shot16_kernel<InT, OutT, 8, 8, WC, true>, prm, u16, 1, dev, st, kWarps16);
+  else if (pl.p2 == 8) launch_ar(two_shot16_kernel<InT, OutT, 4, 8, WC, true>, prm, u16, 1, dev, st, kWarps16);
+  else launch_ar(two_shot16_kernel<InT, OutT, 4, 4, WC, true>, prm, u16, 1, dev, st, kWarps16);
 }
 
 // Phases 2-3 after a fused quantize-and-scatter GEMM.

@@ -36,21 +36,25 @@ void launch_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& 
       reinterpret_cast<const T*>(q.data_ptr()), reinterpret_cast<const T*>(kc.data_ptr()),
       reinterpret_cast<const T*>(vc.data_ptr()), bt.data_ptr<int>(), sl.data_ptr<int>(),
       reinterpret_cast<T*>(out.data_ptr()), part_o.data_ptr<float>(), part_ml.data_ptr<float>(), B, nq, nkv,
-      page_shift, (int)bt.size(1), n_parts, part_tok, scale, st)));
+      page_shift, (int)bt.size(1), n_parts, part_tok, scale, st, q.stride(0))));
 }
 
 }  // namespace
 
-// q [B, nq*hd]; caches [pages, nkv, page, hd]; block_table [B, max_pages] int32;
-// seq_lens [B] int32; out [B, nq*hd].  Context length is bounded by max_pages * page.
+// q [B, nq*hd] (rows may be strided: a view of the fused qkv activation works in place);
+// caches [pages, nkv, page, hd]; block_table [B, max_pages] int32; seq_lens [B] int32;
+// out [B, nq*hd].  Context length is bounded by max_pages * page.
 void attn_decode_cuda(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& bt,
                       const at::Tensor& sl, at::Tensor& out, int64_t nq, int64_t nkv, int64_t hd, double scale) {
-  TORCH_CHECK(q.is_contiguous() && kc.is_contiguous() && vc.is_contiguous() && out.is_contiguous(),
-              "attn_decode: contiguous tensors required");
+  TORCH_CHECK(kc.is_contiguous() && vc.is_contiguous() && out.is_contiguous(),
+              "attn_decode: contiguous caches and output required");
+  TORCH_CHECK(q.dim() == 2 && q.size(1) == nq * hd && q.stride(1) == 1 && q.stride(0) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0,
+              "attn_decode: q must be [B, nq*hd] with unit column stride and 16-byte aligned rows");
   TORCH_CHECK(bt.scalar_type() == at::kInt && sl.scalar_type() == at::kInt, "attn_decode: int32 block table / lens");
   TORCH_CHECK(nq % nkv == 0 && nq / nkv <= kMaxGroup, "attn_decode: GQA group must be <= 8");
   TORCH_CHECK(hd == 128 || hd == 64, "attn_decode: head_dim must be 64 or 128");
-  const int B = (int)(q.numel() / (nq * hd));
+  const int B = (int)q.size(0);
   if (B == 0) return;
   c10::cuda::CUDAGuard guard(q.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();

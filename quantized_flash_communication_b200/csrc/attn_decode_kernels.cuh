@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(kWarps * 32, decode_min_ctas<G>())
 decode_partial_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc,
                       const int* __restrict__ block_table, const int* __restrict__ seq_lens, float* __restrict__ part_o,
                       float* __restrict__ part_ml, int nq, int nkv, int page_shift, int max_pages, int n_parts,
-                      int part_tok, float scale) {
+                      int part_tok, float scale, int64_t q_stride) {
   using Sh = DecodeShape<HD, G>;
   constexpr int LPT = Sh::LPT, EPL = Sh::EPL, NCH = Sh::NCH, TPW = Sh::TPW, NCR = Sh::NCR;
   static_assert(kStageTok % (kWarps * 32 / NCR) == 0, "loader tiling");
@@ -158,7 +158,7 @@ decode_partial_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T
   float2 qv[G][EPL / 2];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    const T* qp = q + ((int64_t)b * nq + kvh * G + g) * HD;
+    const T* qp = q + (int64_t)b * q_stride + (int64_t)(kvh * G + g) * HD;
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
       float2 v[4];
@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 decode_partial_mma_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc,
                           const int* __restrict__ block_table, const int* __restrict__ seq_lens,
                           float* __restrict__ part_o, float* __restrict__ part_ml, int nq, int nkv, int page_shift,
-                          int max_pages, int n_parts, int part_tok, float scale) {
+                          int max_pages, int n_parts, int part_tok, float scale, int64_t q_stride) {
   static_assert(G >= 2 && G <= 8, "mma decode: 2..8 query heads per kv head");
   constexpr int NCR = HD / 8;             // 16-byte chunks per row
   constexpr int KSTEPS = HD / 16;         // k16 steps of q . k
@@ -407,7 +407,7 @@ decode_partial_mma_kernel(const T* __restrict__ q, const T* __restrict__ kc, con
   uint32_t qa0[KSTEPS], qa2[KSTEPS];
   {
     const bool hv = gq < G;
-    const T* qp = q + ((int64_t)b * nq + kvh * G + (hv ? gq : 0)) * HD;
+    const T* qp = q + (int64_t)b * q_stride + (int64_t)(kvh * G + (hv ? gq : 0)) * HD;
 #pragma unroll
     for (int kk = 0; kk < KSTEPS; ++kk) {
       qa0[kk] = hv ? *reinterpret_cast<const uint32_t*>(qp + 16 * kk + 2 * tq) : 0u;
@@ -612,21 +612,23 @@ __global__ void decode_combine_kernel(const float* __restrict__ part_o, const fl
 }
 
 // Both passes on stream st: the tensor-core partial kernel for GQA groups of 2..8 heads,
-// the CUDA-core one for multi-head attention (G = 1), then the merge.
+// the CUDA-core one for multi-head attention (G = 1), then the merge.  Sequence b's query
+// heads start at q + b * q_stride (nq * HD for a packed q; a row of the fused qkv
+// activation is read in place).
 template <typename T, int HD, int G>
 inline cudaError_t decode_launch(const T* q, const T* kc, const T* vc, const int* bt, const int* sl, T* out,
                                  float* part_o, float* part_ml, int B, int nq, int nkv, int page_shift, int max_pages,
-                                 int n_parts, int part_tok, float scale, cudaStream_t st) {
+                                 int n_parts, int part_tok, float scale, cudaStream_t st, int64_t q_stride) {
   const dim3 grid(n_parts, nkv, B);
   cudaError_t err;
   if constexpr (G >= 2) {
     if ((err = decode_mma_prepare<T, HD, G>()) != cudaSuccess) return err;
     decode_partial_mma_kernel<T, HD, G><<<grid, kWarps * 32, decode_mma_smem_bytes<HD>(), st>>>(
-        q, kc, vc, bt, sl, part_o, part_ml, nq, nkv, page_shift, max_pages, n_parts, part_tok, scale);
+        q, kc, vc, bt, sl, part_o, part_ml, nq, nkv, page_shift, max_pages, n_parts, part_tok, scale, q_stride);
   } else {
     if ((err = decode_prepare<T, HD, G>()) != cudaSuccess) return err;
     decode_partial_kernel<T, HD, G><<<grid, kWarps * 32, decode_smem_bytes<HD>(), st>>>(
-        q, kc, vc, bt, sl, part_o, part_ml, nq, nkv, page_shift, max_pages, n_parts, part_tok, scale);
+        q, kc, vc, bt, sl, part_o, part_ml, nq, nkv, page_shift, max_pages, n_parts, part_tok, scale, q_stride);
   }
   if ((err = cudaGetLastError()) != cudaSuccess) return err;
   const int warps = B * nq;

@@ -64,7 +64,7 @@ int launch(const void* q, const void* kc, const void* vc, const int* bt, const i
   const cudaError_t err = decode_launch<T, HD, G>(static_cast<const T*>(q), static_cast<const T*>(kc),
                                                   static_cast<const T*>(vc), bt, sl, static_cast<T*>(out), part_o,
                                                   part_ml, B, nq, nkv, page_shift, max_pages, n_parts, part_tok, scale,
-                                                  st);
+                                                  st, (int64_t)nq * HD);
   return err == cudaSuccess ? QFC_NOALLOC_OK : QFC_NOALLOC_ERR_CUDA;
 }
 

@@ -29,6 +29,8 @@ void quant_all_reduce(const std::vector<std::shared_ptr<Workspace>>& wss, const 
                       bool one_shot, bool quantize_local, double timeout_ms);
 void gemm_all_reduce(const std::shared_ptr<Workspace>& ws, const at::Tensor& a, const at::Tensor& w, at::Tensor& out,
                      int64_t bits, int64_t gs, bool sym, bool scale_fp32, double timeout_ms);
+void argmax_gather(const std::shared_ptr<Workspace>& ws, const at::Tensor& val, const at::Tensor& idx, at::Tensor& out,
+                   double timeout_ms);
 // allreduce_norm.cu
 std::vector<int64_t> ar_plan_rows(int64_t M, int64_t H, int64_t world, int64_t bits, bool scale_fp32);
 void quant_all_reduce_norm(const std::vector<std::shared_ptr<Workspace>>& wss, const std::vector<at::Tensor>& partials,
@@ -41,6 +43,10 @@ void gemm_all_reduce_norm(const std::shared_ptr<Workspace>& ws, const at::Tensor
 // gemm.cu
 at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& out, int64_t epi,
                      const c10::optional<at::Tensor>& residual, double timeout_ms, int64_t max_ctas);
+void gemm_qkv_rope(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, const at::Tensor& pos,
+                   const at::Tensor& cos_sin, const c10::optional<at::Tensor>& k_cache,
+                   const c10::optional<at::Tensor>& v_cache, const c10::optional<at::Tensor>& slots, int64_t nq,
+                   int64_t nkv, double timeout_ms);
 int64_t gemm_status(bool clear);
 // layers.cu
 void rmsnorm_cuda(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& y,
@@ -48,6 +54,9 @@ void rmsnorm_cuda(const at::Tensor& x, const c10::optional<at::Tensor>& residual
 void rope_kv_cuda(at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& cos_sin,
                   const c10::optional<at::Tensor>& k_cache, const c10::optional<at::Tensor>& v_cache,
                   const c10::optional<at::Tensor>& slot_mapping, int64_t nq, int64_t nkv, int64_t hd);
+void rope_kv_decode_cuda(at::Tensor& qkv, const at::Tensor& cos_sin, at::Tensor& k_cache, at::Tensor& v_cache,
+                         const at::Tensor& block_table, const at::Tensor& seq_lens, int64_t nq, int64_t nkv,
+                         int64_t hd);
 void silu_mul_cuda(const at::Tensor& gu, at::Tensor& out);
 void embedding_cuda(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t vocab_start);
 void argmax_cuda(const at::Tensor& logits, at::Tensor& best_val, at::Tensor& best_idx, int64_t idx_offset,
@@ -96,11 +105,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("os_bytes", &qfc::Workspace::os_bytes)
       .def_property_readonly("peers_ready", &qfc::Workspace::peers_ready);
 
+  m.def("gemm_qkv_rope", &qfc::gemm_qkv_rope, "qkv GEMM with RoPE and the KV-cache write in its epilogue",
+        py::arg("a"), py::arg("w"), py::arg("out"), py::arg("pos"), py::arg("cos_sin"), py::arg("k_cache") = py::none(),
+        py::arg("v_cache") = py::none(), py::arg("slots") = py::none(), py::arg("nq"), py::arg("nkv"),
+        py::arg("timeout_ms") = 10000.0);
   m.def("gemm_bf16", &qfc::gemm_bf16, "tcgen05 GEMM a @ b^T with fused epilogue (0 store, 1 swiglu, 2 residual)",
         py::arg("a"), py::arg("b"), py::arg("out") = py::none(), py::arg("epi") = 0,
         py::arg("residual") = py::none(), py::arg("timeout_ms") = 10000.0, py::arg("max_ctas") = 0);
   m.def("gemm_status", &qfc::gemm_status, py::arg("clear") = false);
   m.def("rmsnorm", &qfc::rmsnorm_cuda, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("y"), py::arg("eps"));
+  m.def("rope_kv_decode", &qfc::rope_kv_decode_cuda, "RoPE + paged KV write of one decode token per sequence");
   m.def("rope_kv", &qfc::rope_kv_cuda, py::arg("qkv"), py::arg("pos"), py::arg("cos_sin"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("slot_mapping"), py::arg("nq"), py::arg("nkv"), py::arg("hd"));
   m.def("silu_mul", &qfc::silu_mul_cuda);
@@ -117,6 +131,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("workspaces"), py::arg("ins"), py::arg("outs"), py::arg("bits"), py::arg("group_size"),
         py::arg("sym"), py::arg("scale_fp32"), py::arg("one_shot"), py::arg("quantize_local"),
         py::arg("timeout_ms"));
+  m.def("argmax_gather", &qfc::argmax_gather, "cross-rank argmax of (score, index) pairs (one kernel)");
   m.def("gemm_all_reduce", &qfc::gemm_all_reduce,
         "all_reduce(a @ w^T) with the quantize-and-scatter fused into the GEMM epilogue", py::arg("workspace"),
         py::arg("a"), py::arg("w"), py::arg("out"), py::arg("bits"), py::arg("group_size"), py::arg("sym"),

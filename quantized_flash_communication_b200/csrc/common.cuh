@@ -178,8 +178,14 @@ struct QMath {
     }
   }
   // The code of x as the bit pattern of the float 2^23 + code (code in the low byte).
+  // rhaz(x * inv) + (2^23 + z) is exact while the code is in range; the clamp to
+  // [0, QMAX] then runs on the bit pattern as a signed integer: any result below 2^23
+  // (a negative code, or a negative float) sorts below 0x4B000000, any result above
+  // 2^23 + QMAX sorts above 0x4B000000 + QMAX, since positive floats order like their
+  // bits.  Identical to clamp(rhaz(x * inv) + z, 0, QMAX) + 2^23 for every non-NaN x.
   static QFC_DEV uint32_t codebits(float x, float inv, float z) {
-    return __float_as_uint(fminf(fmaxf(rhaz(x * inv) + z, 0.f), QMAX) + kMagic);
+    const int b = __float_as_int(rhaz(x * inv) + (z + kMagic));
+    return (uint32_t)min(max(b, 0x4b000000), 0x4b000000 + (int)QMAX);
   }
   static QFC_DEV uint32_t code(float x, float inv, float z) { return codebits(x, inv, z) & 0xffu; }
 };
@@ -338,6 +344,16 @@ QFC_DEV void group_minmax16(const uint4& r, int lpg, float& mn, float& mx) {
   else unpack_f16x2(p, a, b);
   mn = -a;
   mx = b;
+}
+
+// ------------------------------------------------------------------------------------
+// Rotary embedding of one (x1, x2) pair (elements i and i + hd/2 of a head) with the
+// position's (cos, sin): the rounding is spelled out so that the standalone RoPE kernel
+// and the GEMM epilogue that fuses it give identical bits.
+// ------------------------------------------------------------------------------------
+QFC_DEV void rope_pair(float x1, float x2, float c, float s, float& y1, float& y2) {
+  y1 = __fmaf_rn(x1, c, -__fmul_rn(x2, s));
+  y2 = __fmaf_rn(x2, c, __fmul_rn(x1, s));
 }
 
 // ------------------------------------------------------------------------------------

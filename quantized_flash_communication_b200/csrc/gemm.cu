@@ -17,6 +17,10 @@
 //                 and writes silu(gate) * up (the reference's act_fn(gate) * up,
 //                 model.py:32-34) as bf16 [M, I]
 //   EPI_RESIDUAL  D = acc + R (bf16), for the residual stream when no all-reduce follows
+//   EPI_ROPE      the qkv projection of a decoder layer: D = acc (bf16) with the rotary
+//                 embedding applied to the q and k heads of each row at its position, and
+//                 the (rotated) k and v heads also written to the paged KV cache (the
+//                 standalone rope_kv kernel's work, done while the next tile's MMAs run)
 //   EPI_QS*       quantize every 128-column group of the bf16-rounded tile and store codes +
 //                 (scale, zero) into the owning rank's reduce-scatter slot over NVLink: the
 //                 first phase of the two-shot all-reduce, overlapped with the GEMM.  The
@@ -68,7 +72,18 @@ constexpr int QS_STAGE_BYTES = 4 * 32 * 256;
 
 // EPI_QS8 / EPI_QS4 / EPI_QS16: quantize each 128-column group of the (bf16-rounded) tile
 // to INT8 / INT4 / raw bf16 and store it into the owner rank's reduce-scatter slot.
-enum Epi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_RESIDUAL = 2, EPI_QS8 = 3, EPI_QS4 = 4, EPI_QS16 = 5 };
+enum Epi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_RESIDUAL = 2, EPI_QS8 = 3, EPI_QS4 = 4, EPI_QS16 = 5,
+                 EPI_ROPE = 6 };
+
+// EPI_ROPE: head_dim 128, so a 256-column tile holds two whole heads.
+struct RopeArgs {
+  const int64_t* pos;       // [M] position of each row
+  const float2* cs;         // [max_position, 64] (cos, sin)
+  __nv_bfloat16* kc;        // [pages, nkv, page, 128] or nullptr (no cache)
+  __nv_bfloat16* vc;
+  const int64_t* slots;     // [M] cache slot page * page_size + offset; < 0 = not cached
+  int nq, nkv, page, page_shift;
+};
 
 constexpr bool is_qs(int epi) { return epi == EPI_QS8 || epi == EPI_QS4 || epi == EPI_QS16; }
 
@@ -87,6 +102,7 @@ struct GemmArgs {
   int* status;
   uint64_t timeout_ns;
   ScatterArgs sc;    // EPI_QS*
+  RopeArgs rope;     // EPI_ROPE
   // split-K (single CTAs, small M): work unit = (tile, split); each unit writes its fp32
   // partial tile, the last unit of a tile (device counter) sums them in split order into
   // TMEM and runs the epilogue.
@@ -508,6 +524,74 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             }
           }
         }
+      } else if constexpr (EPI == EPI_ROPE) {
+        const RopeArgs& ra = args.rope;
+        const int hq = ra.nq, hk = ra.nq + ra.nkv;
+#pragma unroll 1
+        for (int hl = 0; hl < 2; ++hl) {  // the tile's two heads
+          const int hcol = col0 + hl * 128;
+          const int head = hcol >> 7;
+          const bool live = row < args.M && hcol < args.N;
+          const bool rot = head < hk;  // q and k heads rotate, v heads pass through
+          int64_t p_row = 0, slot = -1;
+          if (live) {
+            p_row = ra.pos[row];
+            if (ra.slots != nullptr && head >= hq) slot = ra.slots[row];
+          }
+          __nv_bfloat16* dst = args.D + (int64_t)row * args.ldd + hcol;
+          __nv_bfloat16* cdst = nullptr;
+          if (slot >= 0) {
+            const int64_t pg = ra.page_shift >= 0 ? slot >> ra.page_shift : slot / ra.page;
+            const int64_t off = ra.page_shift >= 0 ? (slot & (ra.page - 1)) : slot % ra.page;
+            const int kvh = head < hk ? head - hq : head - hk;
+            cdst = (head < hk ? ra.kc : ra.vc) + ((pg * ra.nkv + kvh) * (int64_t)ra.page + off) * 128;
+          }
+#pragma unroll 1
+          for (int c = 0; c < 64; c += 32) {  // element i pairs with i + 64
+            uint32_t r1[32], r2[32];
+            tc::tmem_ld_32x32b_x32(taddr + hl * 128 + c, r1);
+            tc::tmem_ld_32x32b_x32(taddr + hl * 128 + 64 + c, r2);
+            tc::tmem_wait_ld();
+            tc::tmem_reg_fence(r1);
+            tc::tmem_reg_fence(r2);
+            if (!live) continue;
+            float x1[32], x2[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {  // the bf16 values the unfused GEMM would store
+              x1[j] = to_f32(from_f32<__nv_bfloat16>(__uint_as_float(r1[j])));
+              x2[j] = to_f32(from_f32<__nv_bfloat16>(__uint_as_float(r2[j])));
+            }
+            if (rot) {
+              const float4* csp = reinterpret_cast<const float4*>(ra.cs + p_row * 64 + c);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float4 a = __ldg(csp + j);  // (cos, sin) of elements 2j and 2j + 1
+                rope_pair(x1[2 * j], x2[2 * j], a.x, a.y, x1[2 * j], x2[2 * j]);
+                rope_pair(x1[2 * j + 1], x2[2 * j + 1], a.z, a.w, x1[2 * j + 1], x2[2 * j + 1]);
+              }
+            }
+            uint4 o1[4], o2[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              o1[j] = make_uint4(pack_bf16(x1[8 * j], x1[8 * j + 1]), pack_bf16(x1[8 * j + 2], x1[8 * j + 3]),
+                                 pack_bf16(x1[8 * j + 4], x1[8 * j + 5]), pack_bf16(x1[8 * j + 6], x1[8 * j + 7]));
+              o2[j] = make_uint4(pack_bf16(x2[8 * j], x2[8 * j + 1]), pack_bf16(x2[8 * j + 2], x2[8 * j + 3]),
+                                 pack_bf16(x2[8 * j + 4], x2[8 * j + 5]), pack_bf16(x2[8 * j + 6], x2[8 * j + 7]));
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              reinterpret_cast<uint4*>(dst + c)[j] = o1[j];
+              reinterpret_cast<uint4*>(dst + 64 + c)[j] = o2[j];
+            }
+            if (cdst != nullptr) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                reinterpret_cast<uint4*>(cdst + c)[j] = o1[j];
+                reinterpret_cast<uint4*>(cdst + 64 + c)[j] = o2[j];
+              }
+            }
+          }
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -724,7 +808,7 @@ void launch_cfg(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& a,
 // CTA pairs serve M >= 256 (a 256-row tile per pair); smaller M runs one CTA per tile.
 template <int EPI>
 void launch(const at::Tensor& A, const at::Tensor& B, at::Tensor* D, const at::Tensor* R, int M, int N, int K,
-            double timeout_ms, int max_ctas, const ScatterArgs* sc = nullptr) {
+            double timeout_ms, int max_ctas, const ScatterArgs* sc = nullptr, const RopeArgs* rope = nullptr) {
   const int dev = A.get_device();
   GemmArgs a;
   a.M = M;
@@ -744,6 +828,8 @@ void launch(const at::Tensor& A, const at::Tensor& B, at::Tensor* D, const at::T
   a.ldd = D ? (int)D->stride(0) : 0;
   std::memset(&a.sc, 0, sizeof(a.sc));
   if (sc) a.sc = *sc;
+  std::memset(&a.rope, 0, sizeof(a.rope));
+  if (rope) a.rope = *rope;
   a.R = R ? reinterpret_cast<const __nv_bfloat16*>(R->data_ptr()) : nullptr;
   a.ldr = R ? (int)R->stride(0) : 0;
   a.status = status_word();
@@ -1130,6 +1216,54 @@ at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& b, const c10::option
     default: TORCH_CHECK(false, "gemm: unknown epilogue ", epi);
   }
   return out;
+}
+
+// qkv = a @ w^T for a decoder layer's fused q/k/v projection (head_dim 128), with the
+// rotary embedding of the q and k heads at positions pos [M] (int64) applied in the
+// epilogue, and the k, v heads written to the paged caches at slots [M] (int64, < 0 = not
+// cached) when k_cache / v_cache / slots are given.  Identical to gemm_bf16 + rope_kv.
+void gemm_qkv_rope(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, const at::Tensor& pos,
+                   const at::Tensor& cos_sin, const c10::optional<at::Tensor>& k_cache,
+                   const c10::optional<at::Tensor>& v_cache, const c10::optional<at::Tensor>& slots, int64_t nq,
+                   int64_t nkv, double timeout_ms) {
+  using namespace gemm;
+  check_operand(a, "a");
+  check_operand(w, "w");
+  check_operand(out, "out");
+  const int M = (int)a.size(0), K = (int)a.size(1), N = (int)w.size(0);
+  TORCH_CHECK(w.size(1) == K && out.size(0) == M && out.size(1) == N, "gemm_qkv_rope: shape mismatch");
+  TORCH_CHECK(N == (nq + 2 * nkv) * 128, "gemm_qkv_rope: head_dim 128 and w = [q; k; v] rows required");
+  TORCH_CHECK(pos.scalar_type() == at::kLong && pos.numel() == M && pos.is_contiguous(), "gemm_qkv_rope: int64 pos [M]");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.dim() == 3 &&
+                  cos_sin.size(1) == 64 && cos_sin.size(2) == 2,
+              "gemm_qkv_rope: fp32 cos/sin table [max_position, 64, 2]");
+  RopeArgs r;
+  std::memset(&r, 0, sizeof(r));
+  r.pos = pos.data_ptr<int64_t>();
+  r.cs = reinterpret_cast<const float2*>(cos_sin.data_ptr());
+  r.nq = (int)nq;
+  r.nkv = (int)nkv;
+  r.page = 1;
+  r.page_shift = -1;
+  const bool cache = slots.has_value() && slots->defined();
+  if (cache) {
+    TORCH_CHECK(k_cache.has_value() && v_cache.has_value(), "gemm_qkv_rope: caches required with slots");
+    TORCH_CHECK(k_cache->dim() == 4 && k_cache->size(1) == nkv && k_cache->size(3) == 128 &&
+                    k_cache->scalar_type() == at::kBFloat16 && k_cache->is_contiguous() &&
+                    v_cache->sizes() == k_cache->sizes() && v_cache->is_contiguous(),
+                "gemm_qkv_rope: bf16 caches [pages, nkv, page, 128]");
+    TORCH_CHECK(slots->scalar_type() == at::kLong && slots->numel() == M && slots->is_contiguous(),
+                "gemm_qkv_rope: int64 slots [M]");
+    r.kc = reinterpret_cast<__nv_bfloat16*>(k_cache->data_ptr());
+    r.vc = reinterpret_cast<__nv_bfloat16*>(v_cache->data_ptr());
+    r.slots = slots->data_ptr<int64_t>();
+    r.page = (int)k_cache->size(2);
+    for (int sh = 0; sh < 31; ++sh)
+      if ((1 << sh) == r.page) r.page_shift = sh;
+  }
+  c10::cuda::CUDAGuard guard(a.device());
+  if (M == 0) return;
+  launch<EPI_ROPE>(a, w, &out, nullptr, M, N, K, timeout_ms, 0, nullptr, &r);
 }
 
 // a @ b^T whose epilogue quantizes every 128-column group (p_bits 8 / 4, or 16 = raw

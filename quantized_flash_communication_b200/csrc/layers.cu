@@ -82,11 +82,17 @@ rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ residual, T* __res
 // the first half): it loads the 16-byte slices j of both halves, rotates them with the
 // (cos, sin) pairs of positions j*8 .. j*8+7 and stores both back (q, k) and into the
 // cache (k, v).  Every access is a 16-byte vector; hd = 64 or 128.
+//
+// Decode form (seq_lens != nullptr, one token per sequence, m = sequence): the position is
+// seq_lens[m] - 1 (the count already includes the new token) and the cache slot comes
+// from the block table in the kernel, so a decode step needs no position / slot tensors;
+// positions at or past max_pages * page are not cached.
 template <typename T, int HD>
 __global__ void rope_kv_kernel(T* __restrict__ qkv, const int64_t* __restrict__ pos, const float2* __restrict__ cs,
                                T* __restrict__ k_cache, T* __restrict__ v_cache,
                                const int64_t* __restrict__ slot_mapping, int64_t M, int nq, int nkv, int page,
-                               int page_shift) {
+                               int page_shift, const int* __restrict__ seq_lens, const int* __restrict__ block_table,
+                               int max_pages) {
   constexpr int HALF = HD / 2, HJ = HALF / 8;
   const uint32_t heads = (uint32_t)(nq + 2 * nkv);
   const int64_t total = M * heads * HJ;
@@ -95,28 +101,31 @@ __global__ void rope_kv_kernel(T* __restrict__ qkv, const int64_t* __restrict__ 
     const uint64_t hh = (uint64_t)(t / HJ);
     const uint32_t h = (uint32_t)(hh % heads);
     const int64_t m = (int64_t)(hh / heads);
+    const int64_t pm = seq_lens != nullptr ? (int64_t)seq_lens[m] - 1 : pos[m];
     T* row = qkv + (m * heads + h) * HD;
     float x1[8], x2[8];
     Vec8IO<T>::load(row + j * 8, x1);
     Vec8IO<T>::load(row + HALF + j * 8, x2);
     if (h < (uint32_t)(nq + nkv)) {
-      const float4* c = reinterpret_cast<const float4*>(cs + pos[m] * HALF + j * 8);
+      const float4* c = reinterpret_cast<const float4*>(cs + pm * HALF + j * 8);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float4 a = c[i];  // (cos, sin) of elements 2i and 2i+1
-        float y1 = x1[2 * i] * a.x - x2[2 * i] * a.y, y2 = x2[2 * i] * a.x + x1[2 * i] * a.y;
-        x1[2 * i] = y1;
-        x2[2 * i] = y2;
-        y1 = x1[2 * i + 1] * a.z - x2[2 * i + 1] * a.w;
-        y2 = x2[2 * i + 1] * a.z + x1[2 * i + 1] * a.w;
-        x1[2 * i + 1] = y1;
-        x2[2 * i + 1] = y2;
+        rope_pair(x1[2 * i], x2[2 * i], a.x, a.y, x1[2 * i], x2[2 * i]);
+        rope_pair(x1[2 * i + 1], x2[2 * i + 1], a.z, a.w, x1[2 * i + 1], x2[2 * i + 1]);
       }
       Vec8IO<T>::store(row + j * 8, x1);
       Vec8IO<T>::store(row + HALF + j * 8, x2);
     }
-    if (h >= (uint32_t)nq && slot_mapping != nullptr) {
-      const int64_t slot = slot_mapping[m];
+    if (h >= (uint32_t)nq && (slot_mapping != nullptr || seq_lens != nullptr)) {
+      int64_t slot;
+      if (seq_lens != nullptr) {
+        slot = (pm >= 0 && pm < (int64_t)max_pages * page)
+                   ? (int64_t)block_table[m * max_pages + (pm / page)] * page + pm % page
+                   : -1;
+      } else {
+        slot = slot_mapping[m];
+      }
       if (slot >= 0) {
         const int64_t pg = page_shift >= 0 ? slot >> page_shift : slot / page;
         const int64_t off = page_shift >= 0 ? slot & (page - 1) : slot % page;
@@ -194,7 +203,7 @@ QFC_DEV float gumbel_noise(uint64_t seed, uint64_t step, int64_t row, int64_t id
 // trick); the last CTA to finish then advances rng[1], so a captured decode step samples
 // afresh on every replay.
 template <typename T, bool SAMPLE>
-__global__ void argmax_kernel(const T* __restrict__ logits, float* __restrict__ best_val, int64_t* __restrict__ best_idx,
+__global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ logits, float* __restrict__ best_val, int64_t* __restrict__ best_idx,
                               int64_t V, int64_t V_valid, int64_t idx_offset, int64_t* __restrict__ rng,
                               float inv_temp, unsigned int* __restrict__ done) {
   const int64_t row = blockIdx.x;
@@ -372,10 +381,54 @@ void rope_kv_cuda(at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& cos_
     const int64_t* sm = cache ? slot_mapping->data_ptr<int64_t>() : nullptr;
     if (hd == 128)
       rope_kv_kernel<scalar_t, 128><<<blocks, threads, 0, st>>>(q, pos.data_ptr<int64_t>(), csp, kcp, vcp, sm, M,
-                                                                 (int)nq, (int)nkv, page, page_shift);
+                                                                 (int)nq, (int)nkv, page, page_shift, nullptr,
+                                                                 nullptr, 0);
     else
       rope_kv_kernel<scalar_t, 64><<<blocks, threads, 0, st>>>(q, pos.data_ptr<int64_t>(), csp, kcp, vcp, sm, M,
-                                                                (int)nq, (int)nkv, page, page_shift);
+                                                                (int)nq, (int)nkv, page, page_shift, nullptr,
+                                                                nullptr, 0);
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Decode step: qkv [B, (nq+2nkv)*hd], one token per sequence at position seq_lens[b] - 1,
+// written to the paged cache through block_table [B, max_pages] (int32).
+void rope_kv_decode_cuda(at::Tensor& qkv, const at::Tensor& cos_sin, at::Tensor& k_cache, at::Tensor& v_cache,
+                         const at::Tensor& block_table, const at::Tensor& seq_lens, int64_t nq, int64_t nkv,
+                         int64_t hd) {
+  TORCH_CHECK(qkv.is_cuda() && qkv.is_contiguous(), "rope_kv_decode: contiguous CUDA qkv");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat, "rope_kv_decode: fp32 cos/sin");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  block_table.is_contiguous() && seq_lens.is_contiguous(),
+              "rope_kv_decode: int32 contiguous block table and sequence lengths");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4, "rope_kv_decode: cache must be [pages, nkv, page, hd]");
+  TORCH_CHECK(hd == 64 || hd == 128, "rope_kv_decode: head_dim must be 64 or 128");
+  const int64_t M = qkv.numel() / ((nq + 2 * nkv) * hd);
+  TORCH_CHECK(seq_lens.numel() == M && block_table.size(0) == M, "rope_kv_decode: one row per sequence");
+  if (M == 0) return;
+  c10::cuda::CUDAGuard guard(qkv.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int page = (int)k_cache.size(2);
+  int page_shift = -1;
+  for (int sh = 0; sh < 31; ++sh)
+    if ((1 << sh) == page) page_shift = sh;
+  const int max_pages = (int)block_table.size(1);
+  const int64_t total = M * (nq + 2 * nkv) * (hd / 16);
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 8);
+  QFC_DISPATCH_16(qkv.scalar_type(), [&] {
+    auto* q = reinterpret_cast<scalar_t*>(qkv.data_ptr());
+    auto* csp = reinterpret_cast<const float2*>(cos_sin.data_ptr());
+    auto* kcp = reinterpret_cast<scalar_t*>(k_cache.data_ptr());
+    auto* vcp = reinterpret_cast<scalar_t*>(v_cache.data_ptr());
+    if (hd == 128)
+      rope_kv_kernel<scalar_t, 128><<<blocks, threads, 0, st>>>(q, nullptr, csp, kcp, vcp, nullptr, M, (int)nq,
+                                                                 (int)nkv, page, page_shift, seq_lens.data_ptr<int>(),
+                                                                 block_table.data_ptr<int>(), max_pages);
+    else
+      rope_kv_kernel<scalar_t, 64><<<blocks, threads, 0, st>>>(q, nullptr, csp, kcp, vcp, nullptr, M, (int)nq,
+                                                                (int)nkv, page, page_shift, seq_lens.data_ptr<int>(),
+                                                                block_table.data_ptr<int>(), max_pages);
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

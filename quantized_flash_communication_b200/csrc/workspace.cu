@@ -34,7 +34,7 @@ Workspace::Workspace(int64_t device, int64_t rank, int64_t world, int64_t rs_byt
   rs_bytes_ = align_up(std::max<int64_t>(rs_bytes, 256), 4096);
   ag_bytes_ = align_up(std::max<int64_t>(ag_bytes, 256), 4096);
   os_bytes_ = align_up(std::max<int64_t>(os_bytes, 256), 4096);
-  total_bytes_ = kFlagBytes + rs_bytes_ + ag_bytes_ + 2 * os_bytes_;
+  total_bytes_ = kFlagBytes + kArgmaxBytes + rs_bytes_ + ag_bytes_ + 2 * os_bytes_;
   DeviceScope scope((int)device);
   cuda_check(cudaMalloc(&base_, total_bytes_), "cudaMalloc(workspace)");
   cuda_check(cudaMemset(base_, 0, kFlagBytes), "cudaMemset(flags)");

@@ -7,6 +7,7 @@
 //
 // Buffer layout (byte offsets, identical on every rank):
 //   [0, kFlagBytes)                     flags[phase][block][src_rank]  (uint32)
+//   [kFlagBytes, + kArgmaxBytes)        argmax gather slots, double-buffered by epoch parity
 //   [rs_off, rs_off + rs_bytes)         two-shot reduce-scatter slots (one per source rank)
 //   [ag_off, ag_off + ag_bytes)         two-shot all-gather slots      (one per source rank)
 //   [os_off, os_off + 2 * os_bytes)     one-shot slots, double-buffered by epoch parity
@@ -28,12 +29,15 @@ namespace qfc {
 
 constexpr int kMaxRanks = 8;
 constexpr int kMaxBlocks = 1024;
-constexpr int kFlagPhases = 4;   // 0 reduce-scatter, 1 all-gather, 2 one-shot, 3 GEMM-fused scatter
-constexpr int kEpochAlgos = 4;   // per-algorithm epoch counters
+constexpr int kFlagPhases = 5;   // 0 reduce-scatter, 1 all-gather, 2 one-shot, 3 GEMM-fused scatter, 4 argmax
+constexpr int kEpochAlgos = 5;   // per-algorithm epoch counters
 constexpr int64_t kFlagBytes = (int64_t)kFlagPhases * kMaxBlocks * kMaxRanks * sizeof(uint32_t);
+// Cross-rank argmax: up to kArgmaxRows (score, index) pairs of 8 bytes per source rank.
+constexpr int64_t kArgmaxRows = 512;
+constexpr int64_t kArgmaxBytes = 2 * kMaxRanks * kArgmaxRows * 8;
 
-enum FlagPhase : int { PH_RS = 0, PH_AG = 1, PH_OS = 2, PH_GEMM = 3 };
-enum EpochAlgo : int { ALG_TWO_SHOT = 0, ALG_ONE_SHOT = 1, ALG_GEMM_RS = 2, ALG_GEMM_AG = 3 };
+enum FlagPhase : int { PH_RS = 0, PH_AG = 1, PH_OS = 2, PH_GEMM = 3, PH_ARGMAX = 4 };
+enum EpochAlgo : int { ALG_TWO_SHOT = 0, ALG_ONE_SHOT = 1, ALG_GEMM_RS = 2, ALG_GEMM_AG = 3, ALG_ARGMAX = 4 };
 
 inline int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
@@ -61,9 +65,10 @@ class Workspace {
   int64_t rs_bytes() const { return rs_bytes_; }
   int64_t ag_bytes() const { return ag_bytes_; }
   int64_t os_bytes() const { return os_bytes_; }
-  int64_t rs_off() const { return kFlagBytes; }
-  int64_t ag_off() const { return kFlagBytes + rs_bytes_; }
-  int64_t os_off() const { return kFlagBytes + rs_bytes_ + ag_bytes_; }
+  int64_t argmax_off() const { return kFlagBytes; }
+  int64_t rs_off() const { return kFlagBytes + kArgmaxBytes; }
+  int64_t ag_off() const { return rs_off() + rs_bytes_; }
+  int64_t os_off() const { return rs_off() + rs_bytes_ + ag_bytes_; }
   bool peers_ready() const { return peers_ready_; }
 
   char* base() const { return base_; }

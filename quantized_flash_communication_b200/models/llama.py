@@ -172,6 +172,8 @@ class TPContext:
         if self.world == 1:
             return idx
         B = val.numel()
+        if self.ar is not None and B <= 512:
+            return self.ar.argmax(val, idx)  # one kernel over peer memory
         buf = torch.zeros(self.world, B, 2, dtype=torch.float32, device=val.device)
         buf[self.rank, :, 0] = val
         buf[self.rank, :, 1] = idx.to(torch.float32)
@@ -455,12 +457,22 @@ class LlamaTP(nn.Module):
         lay = self.model.layers[li]
         eps = cfg.rms_eps
         t = self.timer
-        with maybe_region(t, "qkv_gemm"):
-            qkv = G.linear(x, lay.self_attn.qkv_fused)
         kc = cache.k[li] if cache is not None else None
         vc = cache.v[li] if cache is not None else None
-        with maybe_region(t, "rope_kv"):
-            L.rope_kv(qkv, pos, self.cos_sin, self.nq, self.nkv, self.hd, kc, vc, slots)
+        if pos is not None and self.hd == 128 and x.shape[0] > 64:
+            # prefill: RoPE and the KV-cache write run in the qkv GEMM's epilogue
+            with maybe_region(t, "qkv_gemm+rope_kv"):
+                qkv = G.linear_qkv_rope(x, lay.self_attn.qkv_fused, pos, self.cos_sin, self.nq, self.nkv, kc, vc,
+                                        slots)
+        else:
+            with maybe_region(t, "qkv_gemm"):
+                qkv = G.linear(x, lay.self_attn.qkv_fused)
+            with maybe_region(t, "rope_kv"):
+                if pos is None:  # decode: position seq_lens - 1 and the cache slot, in the kernel
+                    L.rope_kv_decode(qkv, self.cos_sin, self.nq, self.nkv, self.hd, kc, vc, cache.block_table,
+                                     cache.seq_lens)
+                else:
+                    L.rope_kv(qkv, pos, self.cos_sin, self.nq, self.nkv, self.hd, kc, vc, slots)
         with maybe_region(t, "attention"):
             o = attn_fn(qkv, li)
         if sp:
@@ -577,26 +589,20 @@ class LlamaTP(nn.Module):
     def decode_step(self, tokens: torch.Tensor, cache: KVCache, sampler: Optional[Sampler] = None) -> torch.Tensor:
         """One token per sequence: appends to the cache and returns the next tokens [B]
         (greedy, or drawn by ``sampler``)."""
-        B = tokens.numel()
         cfg = self.cfg
         t = self.timer
-        with maybe_region(t, "positions+slots"):
-            pos = cache.seq_lens.to(torch.int64)
-            b_idx = torch.arange(B, device=self.device)
-            slots = cache.slots(b_idx, pos)
         with maybe_region(t, "embedding+rmsnorm"):
             h = L.embedding(tokens.reshape(-1), self.model.embed_tokens.weight)
             x = L.rmsnorm(h, self.model.layers[0].input_layernorm.weight, cfg.rms_eps)
         cache.seq_lens.add_(1)
         nqr = self.nq * self.hd
 
-        def attn(qkv, li):
-            q = qkv[:, :nqr].contiguous()
-            return A.decode_attention(q, cache.k[li], cache.v[li], cache.block_table, cache.seq_lens, self.nq,
-                                      self.nkv, self.hd)
+        def attn(qkv, li):  # q is read in place from the fused qkv rows
+            return A.decode_attention(qkv[:, :nqr], cache.k[li], cache.v[li], cache.block_table, cache.seq_lens,
+                                      self.nq, self.nkv, self.hd)
 
         for li in range(cfg.num_layers):
-            x = self._layer(li, h, x, attn, pos, slots, cache)
+            x = self._layer(li, h, x, attn, None, None, cache)
         with maybe_region(t, "lm_head+argmax"):
             return self._head(x, sampler)
 

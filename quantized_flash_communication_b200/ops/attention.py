@@ -42,10 +42,11 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
                      out: torch.Tensor | None = None) -> torch.Tensor:
     """One query token per sequence over its paged cache.
 
-    q [B, nq*hd]; caches [pages, nkv, page, hd]; block_table [B, max_pages] int32;
-    seq_lens [B] int32 (tokens in the cache, including the current one).
+    q [B, nq*hd] (rows may be strided, e.g. the q columns of the fused qkv activation);
+    caches [pages, nkv, page, hd]; block_table [B, max_pages] int32; seq_lens [B] int32
+    (tokens in the cache, including the current one).
     """
-    o = torch.empty_like(q) if out is None else out
+    o = torch.empty(q.shape[0], nq * hd, dtype=q.dtype, device=q.device) if out is None else out
     ext().attn_decode(q, k_cache, v_cache, block_table, seq_lens, o, nq, nkv, hd, 1.0 / hd ** 0.5)
     return o
 

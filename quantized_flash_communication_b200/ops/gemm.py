@@ -10,7 +10,8 @@ import torch
 
 from .._ext import ext
 
-__all__ = ["linear", "linear_swiglu", "linear_residual", "gemm_status", "EPI_STORE", "EPI_SWIGLU", "EPI_RESIDUAL"]
+__all__ = ["linear", "linear_swiglu", "linear_residual", "linear_qkv_rope", "gemm_status", "EPI_STORE", "EPI_SWIGLU",
+           "EPI_RESIDUAL"]
 
 EPI_STORE, EPI_SWIGLU, EPI_RESIDUAL = 0, 1, 2
 
@@ -37,6 +38,18 @@ def linear_residual(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
     """``x @ w.T + residual`` (``out`` may alias ``residual``)."""
     y = ext().gemm_bf16(_2d(x), w, None if out is None else _2d(out), EPI_RESIDUAL, _2d(residual))
     return y.view(*x.shape[:-1], w.shape[0])
+
+
+def linear_qkv_rope(x: torch.Tensor, w_qkv: torch.Tensor, pos: torch.Tensor, cos_sin: torch.Tensor, nq: int, nkv: int,
+                    k_cache: Optional[torch.Tensor] = None, v_cache: Optional[torch.Tensor] = None,
+                    slots: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``x @ w_qkv.T`` with the rotary embedding of its q and k heads applied at ``pos`` and
+    its k, v heads written to the paged caches at ``slots``, all in the GEMM's epilogue
+    (head_dim 128).  Same result as :func:`linear` followed by ``layers.rope_kv``."""
+    x2 = _2d(x)
+    y = torch.empty(x2.shape[0], w_qkv.shape[0], dtype=x.dtype, device=x.device) if out is None else _2d(out)
+    ext().gemm_qkv_rope(x2, w_qkv, y, pos, cos_sin, k_cache, v_cache, slots, nq, nkv)
+    return y.view(*x.shape[:-1], w_qkv.shape[0])
 
 
 def gemm_status(clear: bool = False) -> int:

@@ -43,6 +43,14 @@ def rope_kv(qkv: torch.Tensor, pos: torch.Tensor, cos_sin: torch.Tensor, nq: int
     ext().rope_kv(qkv, pos, cos_sin, k_cache, v_cache, slot_mapping, nq, nkv, hd)
 
 
+def rope_kv_decode(qkv: torch.Tensor, cos_sin: torch.Tensor, nq: int, nkv: int, hd: int, k_cache: torch.Tensor,
+                   v_cache: torch.Tensor, block_table: torch.Tensor, seq_lens: torch.Tensor) -> None:
+    """In-place RoPE of one decode token per sequence (``qkv [B, (nq+2nkv)*hd]``) at position
+    ``seq_lens[b] - 1``, and its k, v written to the paged cache through ``block_table``;
+    positions and cache slots are computed inside the kernel."""
+    ext().rope_kv_decode(qkv, cos_sin, k_cache, v_cache, block_table, seq_lens, nq, nkv, hd)
+
+
 def silu_mul(gu: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     I = gu.shape[-1] // 2
     y = torch.empty(*gu.shape[:-1], I, dtype=gu.dtype, device=gu.device) if out is None else out

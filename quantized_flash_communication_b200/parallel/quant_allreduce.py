@@ -193,6 +193,13 @@ class QuantAllReduce(_Base):
         ext().gemm_all_reduce(self.ws.native, a2, w, out, bits, 128, qt == "sym", fp32, self.timeout_ms)
         return out
 
+    def argmax(self, val: torch.Tensor, idx: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Global argmax per row from every rank's (score fp32, global index int64) pair:
+        the highest score wins, ties go to the lower rank (one kernel, at most 512 rows)."""
+        out = torch.empty(val.numel(), dtype=torch.int64, device=val.device) if out is None else out
+        ext().argmax_gather(self.ws.native, val.contiguous(), idx.contiguous(), out, self.timeout_ms)
+        return out
+
     def check(self, synchronize: bool = True):
         self.ws.check(synchronize)
 

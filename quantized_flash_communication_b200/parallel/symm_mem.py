@@ -29,7 +29,7 @@ class CommTimeoutError(RuntimeError):
     """A fused cross-GPU kernel gave up waiting for a peer's flag."""
 
 
-_PHASES = {0: "reduce-scatter", 1: "all-gather", 2: "one-shot", 3: "gemm-scatter"}
+_PHASES = {0: "reduce-scatter", 1: "all-gather", 2: "one-shot", 3: "gemm-scatter", 4: "argmax"}
 
 
 def default_timeout_ms() -> float:

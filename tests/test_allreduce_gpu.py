@@ -37,6 +37,10 @@ CASES = [
     (1, 8, 128, "asym", (5, 4096), "two_shot"),
     (3, 8, 128, "asym", (37, 4096), "two_shot"),   # generic (runtime world size) kernels
     (5, 6, 64, "sym", (9, 1000), "two_shot"),
+    (4, 8, 16, "asym", (6, 4096), "two_shot"),     # one lane per group
+    (2, 4, 256, "sym", (10, 4096), "two_shot"),    # two groups per 512-element unit
+    (3, 8, 8, "asym", (5, 1000), "two_shot"),      # 8-element groups: 8-per-lane kernel
+    (8, 6, 32, "asym", (33, 8192), "two_shot"),
     (3, 4, 128, "asym", (5, 4096), "one_shot"),
     (2, 8, 128, "asym", (1, 4096), "one_shot"),
     (8, 8, 128, "asym", (64, 4096), "one_shot"),

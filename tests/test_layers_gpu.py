@@ -95,3 +95,30 @@ def test_argmax_first_maximum(cuda_device, V, dtype):
     bv, bi = L.argmax(logits)
     assert torch.equal(bi, cols[:, 0])
     assert torch.equal(bv.float(), torch.full_like(bv.float(), float(torch.tensor(hi).to(dtype))))
+
+
+@pytest.mark.parametrize("M,nq,nkv,page", [(100, 8, 2, 16), (513, 4, 4, 64), (2048, 32, 8, 64)])
+def test_qkv_gemm_with_fused_rope_matches_unfused(cuda_device, M, nq, nkv, page):
+    """The qkv GEMM's RoPE + KV-cache epilogue equals the GEMM followed by rope_kv, bit for bit."""
+    from quantized_flash_communication_b200.ops import gemm as G
+    hd, K = 128, 1024
+    g = torch.Generator(device="cpu").manual_seed(M)
+    x = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    w = (torch.randn((nq + 2 * nkv) * hd, K, generator=g) * 0.03).to(cuda_device, torch.bfloat16)
+    cs = L.rope_cos_sin(8192, hd, 500000.0, cuda_device)
+    pos = torch.randint(0, 8192, (M,), generator=g).to(cuda_device)
+    pages = (M + page - 1) // page + 2
+    slots = torch.randperm(pages * page, generator=g)[:M].to(cuda_device)
+    slots[::11] = -1
+    kc1 = torch.zeros(pages, nkv, page, hd, device=cuda_device, dtype=torch.bfloat16)
+    vc1 = torch.zeros_like(kc1)
+    kc2, vc2 = kc1.clone(), vc1.clone()
+    ref = G.linear(x, w)
+    L.rope_kv(ref, pos, cs, nq, nkv, hd, kc1, vc1, slots)
+    got = G.linear_qkv_rope(x, w, pos, cs, nq, nkv, kc2, vc2, slots)
+    torch.cuda.synchronize()
+    assert G.gemm_status() == 0
+    assert torch.equal(got, ref)
+    assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)
+    got2 = G.linear_qkv_rope(x, w, pos, cs, nq, nkv)  # no cache
+    assert torch.equal(got2, ref)
