@@ -354,42 +354,14 @@ def run_ours(args):
 # ------------------------------------------------------------------------------------------
 def run_reference(args):
     import torch
-    ref = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isfile(os.path.join(ref, "communication.py")):
+    sys.path.insert(0, ROOT)
+    from quantized_flash_communication_b200.benchmarks.reference_arm import build_reference_model, reference_available
+    if not reference_available():
         return 0, {"impl": "reference", "unavailable": "baseline/_ref is missing (copy the reference's 7 .py files)"}
     rank, world, dev = _dist_init(args)
-    # The reference's main.py imports a `utils` module that it does not ship (main.py:17);
-    # provide the three names it imports so its own inject_ultimate_layers can be used.
-    stub = types.ModuleType("utils")
-    stub.setup_ddp = lambda *a, **k: None
-    stub.cleanup_ddp = lambda *a, **k: None
-    stub.set_seed = lambda s=42: torch.manual_seed(s)
-    sys.modules["utils"] = stub
-    sys.path.insert(0, ref)
-    import main as ref_main  # noqa: E402  (reference, unmodified)
-    from transformers import LlamaConfig as HFConfig, LlamaForCausalLM
-
-    sys.path.insert(1, ROOT)
     from quantized_flash_communication_b200.models.config import get_config
     cfg = get_config(args.model)
-    hf = HFConfig(hidden_size=cfg.hidden_size, intermediate_size=cfg.intermediate_size,
-                  num_hidden_layers=cfg.num_layers, num_attention_heads=cfg.num_heads,
-                  num_key_value_heads=cfg.num_kv_heads, vocab_size=cfg.vocab_size, rms_norm_eps=cfg.rms_eps,
-                  rope_theta=cfg.rope_theta, max_position_embeddings=cfg.max_position, initializer_range=0.02,
-                  tie_word_embeddings=False)
-    torch.manual_seed(1234)
-    prev = torch.get_default_dtype()
-    torch.set_default_dtype(torch.float16)
-    with torch.device(dev):
-        model = LlamaForCausalLM(hf)
-    torch.set_default_dtype(prev)
-    model.eval()
-    ref_main.inject_ultimate_layers(model, rank, world)
-    for layer in model.model.layers:
-        layer.mlp.mode = "flash"
-        layer.mlp.bits = args.bits
-        layer.mlp.group_size = args.group_size
-        layer.mlp.quant_type = args.quant_type
+    model = build_reference_model(cfg, dev, rank, world, args.bits, args.group_size, args.quant_type)
     B, S = args.batch, args.seq
     g = torch.Generator(device="cpu").manual_seed(42)
     ids_host = torch.randint(0, cfg.vocab_size, (B, S), generator=g).pin_memory()

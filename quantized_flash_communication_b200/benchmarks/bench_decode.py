@@ -10,6 +10,13 @@ Random-init weights N(0, 0.02), uniformly random token ids.  The context is pref
 sequence, one CUDA graph replay that includes the quantized all-reduces and the argmax
 combine) is timed over ``new - 1`` steps after ``--warmup`` untimed steps.  Rank 0 prints one
 JSON line: TTFT, per-token latency and decode tokens/s for the whole batch.
+
+``--impl reference`` times the reference's own path on the same shapes: Hugging Face
+``generate`` (the call of the reference's QA test, inference.py:29-36) on a random-init
+``LlamaForCausalLM`` with the reference's injected tensor-parallel MLPs and its
+``flash_all_reduce`` (benchmarks/reference_arm.py), greedy, fp16.  TTFT is a
+``generate`` of one token; the per-token latency is (a ``generate`` of ``new`` tokens minus
+TTFT) / (new - 1), both CUDA-event timed, max over ranks.
 """
 from __future__ import annotations
 
@@ -39,6 +46,59 @@ def _barrier():
         dist.barrier()
 
 
+def _run_reference(args, cfg, rank, world, dev):
+    from .reference_arm import build_reference_model, reference_available
+    if not reference_available():
+        if rank == 0:
+            print(json.dumps({"benchmark": "tp_decode", "impl": "reference", "unavailable": "baseline/_ref is missing"}))
+        return
+    if not dist.is_initialized():  # the reference's all-reduce needs a process group, also for one rank
+        import os
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29541")
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
+    B, S = args.batch, args.ctx
+    model = build_reference_model(cfg, dev, rank, world, bits=args.bits, group_size=args.group_size)
+    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(1)).to(dev)
+    mask = torch.ones_like(ids)
+
+    def gen(n):
+        with torch.no_grad():
+            return model.generate(ids, attention_mask=mask, max_new_tokens=n, min_new_tokens=n, do_sample=False,
+                                  pad_token_id=0)
+
+    gen(2)  # warm-up: the reference's Triton / JIT kernels compile here
+    torch.cuda.synchronize()
+    _barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    gen(1)
+    e.record()
+    torch.cuda.synchronize()
+    ttft = _max(s.elapsed_time(e), dev)
+    _barrier()
+    sampler = ClockSampler(list(range(world)) if world > 1 else [dev.index]) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    s.record()
+    out = gen(args.new)
+    e.record()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.__exit__(None, None, None)
+    total = _max(s.elapsed_time(e), dev)
+    per_tok = (total - ttft) / max(1, args.new - 1)
+    if rank == 0:
+        print(json.dumps({
+            "benchmark": "tp_decode", "impl": "reference", "model": cfg.name, "n_gpus": world, "batch": B, "ctx": S,
+            "new_tokens": args.new, "generated": int(out.shape[1] - S),
+            "allreduce": f"reference flash_all_reduce INT{args.bits} g{args.group_size} asym (MLP only)",
+            "ttft_ms": ttft, "per_token_ms": per_tok, "decode_tokens_per_s": B * 1000.0 / per_tok, "dtype": "fp16",
+            "api": "transformers generate (greedy) + reference inject_ultimate_layers + flash_all_reduce",
+            "clocks": sampler.summary() if sampler else None,
+            "data": "synthetic: uniform random token ids, random-init N(0,0.02) weights"}), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="llama3-8b")
@@ -52,11 +112,17 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (debug only)")
     ap.add_argument("--breakdown", action="store_true",
                     help="also time eager decode steps per operator (CUDA-event regions, max over ranks)")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     args = ap.parse_args(argv)
     rank, world, dev = init_distributed()
     cfg = get_config(args.model)
     if args.layers:
         cfg = cfg.with_layers(args.layers)
+    if args.impl == "reference":
+        _run_reference(args, cfg, rank, world, dev)
+        if dist.is_available() and dist.is_initialized():
+            dist.destroy_process_group()
+        return
     B, S = args.batch, args.ctx
     tp = TPContext(None, dev, ar_backend=args.ar_backend, bits=args.bits, group_size=args.group_size,
                    reserve_tokens=B * S, hidden_size=cfg.hidden_size)

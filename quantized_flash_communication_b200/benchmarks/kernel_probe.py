@@ -6,6 +6,15 @@
     python -m quantized_flash_communication_b200.benchmarks.kernel_probe allreduce_norm 2 8192 4096 8
     python -m quantized_flash_communication_b200.benchmarks.kernel_probe quantize 67108864
     python -m quantized_flash_communication_b200.benchmarks.kernel_probe decode 64 4096 16 4
+    python -m quantized_flash_communication_b200.benchmarks.kernel_probe rmsnorm 8192 4096
+    python -m quantized_flash_communication_b200.benchmarks.kernel_probe rope_decode 64 32 8
+    python -m quantized_flash_communication_b200.benchmarks.kernel_probe silu_mul 8192 11008
+    python -m quantized_flash_communication_b200.benchmarks.kernel_probe pack 67108864
+    python -m quantized_flash_communication_b200.benchmarks.kernel_probe unpack 67108864
+    python -m quantized_flash_communication_b200.benchmarks.kernel_probe oneshot 8 64 4096 8
+    python -m quantized_flash_communication_b200.benchmarks.kernel_probe gemm_qs8 8192 4096 4096
+    python -m quantized_flash_communication_b200.benchmarks.kernel_probe gemm_small 64 4096 14336
+    python -m quantized_flash_communication_b200.benchmarks.kernel_probe qkv_rope 8192 4096 32 32
 
 Each subcommand runs ``--iters`` launches (default 3) after one warm-up and prints the
 median device time; ``allreduce`` and ``allreduce_norm`` (the sequence-parallel
@@ -23,7 +32,9 @@ from .timing import median, time_fn
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "attention", "allreduce", "allreduce_norm", "quantize", "decode"])
+    ap.add_argument("kernel", choices=["gemm", "attention", "allreduce", "allreduce_norm", "quantize", "decode",
+                                       "rmsnorm", "rope_decode", "silu_mul", "pack", "unpack", "oneshot", "gemm_qs8",
+                                       "gemm_small", "qkv_rope"])
     ap.add_argument("shape", nargs="*", type=int)
     ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args(argv)
@@ -62,6 +73,73 @@ def main(argv=None):
         (n,) = args.shape or (1 << 26,)
         x = torch.randn(n, device=dev, dtype=torch.bfloat16)
         fn, work = (lambda: Q.quantize(x, 8, 128)), float(n)
+    elif args.kernel == "rmsnorm":
+        from ..ops import layers as L
+        M, H = args.shape or (8192, 4096)
+        x = torch.randn(M, H, device=dev, dtype=torch.bfloat16)
+        r = torch.randn(M, H, device=dev, dtype=torch.bfloat16)
+        w = torch.ones(H, device=dev, dtype=torch.bfloat16)
+        y = torch.empty_like(x)
+        fn, work = (lambda: L.rmsnorm(x, w, 1e-5, residual=r, out=y)), float(M * H * 2 * 4)  # bytes: x, r in; r, y out
+    elif args.kernel == "rope_decode":
+        from ..ops import layers as L
+        B, nq, nkv = args.shape or (64, 32, 8)
+        hd, page, pps = 128, 64, 64
+        qkv = torch.randn(B, (nq + 2 * nkv) * hd, device=dev, dtype=torch.bfloat16)
+        cs = L.rope_cos_sin(8192, hd, 500000.0, dev)
+        kc = torch.zeros(B * pps, nkv, page, hd, device=dev, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        bt = torch.arange(B * pps, device=dev, dtype=torch.int32).view(B, pps)
+        lens = torch.full((B,), 1000, device=dev, dtype=torch.int32)
+        fn = lambda: L.rope_kv_decode(qkv, cs, nq, nkv, hd, kc, vc, bt, lens)  # noqa: E731
+        work = float(qkv.numel() * 2 + B * nq * hd * 2 + 2 * B * nkv * hd * 2)  # bytes
+    elif args.kernel == "silu_mul":
+        from ..ops import layers as L
+        M, I = args.shape or (8192, 11008)
+        gu = torch.randn(M, 2 * I, device=dev, dtype=torch.bfloat16)
+        y = torch.empty(M, I, device=dev, dtype=torch.bfloat16)
+        fn, work = (lambda: L.silu_mul(gu, out=y)), float(M * I * 2 * 3)
+    elif args.kernel in ("pack", "unpack"):
+        from .. import kernels_jit as KJ
+        (n,) = args.shape or (1 << 26,)
+        codes = torch.randint(0, 16, (n,), device=dev, dtype=torch.int8)
+        packed = KJ.pack_int4(codes)
+        if args.kernel == "pack":
+            fn, work = (lambda: KJ.pack_int4(codes)), float(n + n // 2)
+        else:
+            fn, work = (lambda: KJ.unpack_int4(packed, codes.shape)), float(n // 2 + n * 2)
+    elif args.kernel == "oneshot":
+        from ..parallel import EmulatedQuantAllReduce
+        W, T, H, bits = args.shape or (8, 64, 4096, 8)
+        ar = EmulatedQuantAllReduce(W, dev, bits=bits, group_size=128, algo="one_shot")
+        xs = [torch.randn(T, H, device=dev, dtype=torch.bfloat16) for _ in range(W)]
+        outs = [torch.empty_like(x) for x in xs]
+        fn, work = (lambda: ar(xs, outs)), float(W * T * H)
+    elif args.kernel == "gemm_qs8":
+        from ..parallel import QuantAllReduce
+        M, N, K = args.shape or (8192, 4096, 4096)
+        ar = QuantAllReduce(None, dev, bits=8, group_size=128, algo="two_shot")  # one rank: own slots
+        a = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+        b = torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.02
+        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        fn, work = (lambda: ar.gemm_all_reduce(a, b, out=out)), 2.0 * M * N * K
+    elif args.kernel == "gemm_small":
+        from ..ops import gemm as G
+        M, N, K = args.shape or (64, 4096, 14336)
+        a = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+        b = torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.02
+        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        fn, work = (lambda: G.linear(a, b, out=out)), float(N * K * 2)  # weight bytes streamed
+    elif args.kernel == "qkv_rope":
+        from ..ops import gemm as G
+        from ..ops import layers as L
+        M, K, nq, nkv = args.shape or (8192, 4096, 32, 32)
+        a = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+        w = torch.randn((nq + 2 * nkv) * 128, K, device=dev, dtype=torch.bfloat16) * 0.02
+        pos = torch.arange(M, device=dev) % 1024
+        cs = L.rope_cos_sin(4096, 128, 10000.0, dev)
+        out = torch.empty(M, w.shape[0], device=dev, dtype=torch.bfloat16)
+        fn, work = (lambda: G.linear_qkv_rope(a, w, pos, cs, nq, nkv, out=out)), 2.0 * M * w.shape[0] * K
     else:
         from ..ops.attention import decode_attention
         B, ctx, nq, nkv = args.shape or (64, 4096, 16, 4)

@@ -5,18 +5,30 @@
 // (after RoPE).  Q and K tiles are K-major operands (head dim contiguous); V tiles, loaded
 // the same way, are the MN-major B operand of P V, so nothing is transposed.
 //
-// Persistent: one CTA per SM walks (128-query tile, query head, sequence) work items,
-// heaviest first; 10 warps:
-//   warp 0      TMA: Q once, then K_j and V^T_j into a 2-stage ring;
-//   warp 1      TMEM allocation and MMA issue: S_j = Q K_j^T (M=N=128, K=hd) into one of two
-//               TMEM S buffers, then O_j = P_j V_j (M=128, N=hd, K=128) into one of two
-//               TMEM O buffers (fresh accumulation per tile);
-//   warps 2-5   softmax: thread = query row; reads its S row from TMEM, applies the causal
-//               and sequence-end masks, keeps the running max / sum, writes P_j (bf16) into
-//               swizzled shared memory for the next MMA and the rescale factor alpha_j;
-//   warps 6-9   correction: thread = query row; O += alpha_j * O + O_j in registers, and the
-//               final O / l to global memory.
-// K/V tiles above the diagonal are skipped.  Every mbarrier wait is bounded.
+// Persistent: one CTA per SM walks work items (a pair of adjacent 128-query tiles A and B
+// of one head of one sequence), heaviest first.  Both tiles share every K / V tile load.
+// 10 warps:
+//   warp 0      TMA: Q_A and Q_B once per item, then K_j and V_j into 2-stage rings;
+//   warp 1      TMEM allocation and MMA issue.  Per KV tile j the order is
+//                 PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)
+//               with S = Q K_j^T (M = N = 128, K = hd) and O += P V_j (M = 128, N = hd,
+//               K = 128) accumulated in TMEM, P read from TMEM as the A operand, so tile
+//               A's softmax of j + 1 overlaps the tensor core's work on B and the other way
+//               round (ping-pong);
+//   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B: thread = query row.  It
+//               reads its S row from TMEM, masks (causal, sequence end), keeps the row's
+//               reference maximum and sum, and writes P (bf16 pairs) back over the first 64
+//               columns of its S row.
+//               The reference maximum moves only when a new maximum exceeds it by more
+//               than 2^8 (log2 domain); only then is the O row in TMEM rescaled, by the
+//               same thread, before P is released.  After the last tile the thread reads
+//               its O row, divides by the sum and stores bf16.
+// TMEM (512 columns): S_A (then P_A) | S_B (then P_B) | O_A | O_B.  Shared memory: Q_A,
+// Q_B, K[2], V[2] (6 x 32 KiB).  The tensor pipe runs one thread's MMAs in order, so S_t of
+// tile j + 1 (issued after PV_t of tile j) never overwrites P_t before it is read, and the
+// completion of S_t(j + 1) implies that of PV_t(j).  K / V tiles above the diagonal are
+// skipped; tile A has one tile fewer than B.  Every mbarrier wait is bounded; on expiry the
+// CTA records an error, drains its copies and MMAs and frees TMEM.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAException.h>
@@ -39,12 +51,14 @@ constexpr int HALF_BYTES = TILE_BYTES / 2;
 constexpr int NUM_THREADS = 320;
 constexpr uint32_t IDESC = tc::idesc_f16(128, 128, true);           // S = Q K^T, both K-major
 constexpr uint32_t IDESC_PV = tc::idesc_f16(128, 128, true, true);  // O = P V, V MN-major
-// smem: Q | K[2] | Vt[2] | P[2] | barriers + alpha/l
-constexpr int SMEM_BYTES = 7 * TILE_BYTES + 1024 + 2048;
+// smem: Q[2] | K[2] | V[2] | barriers
+constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 2048;
+// log2-domain growth of the row maximum tolerated before O is rescaled (P <= 2^8)
+constexpr float kRescaleLog2 = 8.f;
 
 struct Args {
   int B, S, nq, nkv, group;
-  int q_tiles;
+  int q_tiles, q_pairs;
   float scale_log2;
   __nv_bfloat16* out;  // [B*S, nq*HD]
   int* status;
@@ -62,71 +76,60 @@ QFC_DEV float ex2(float x) {
   return y;
 }
 
-QFC_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// Byte offset of the 16-byte chunk `c` (0..7) of row `r` inside a 128-byte-swizzled
-// K-major tile of 64 bf16 columns: rows are 128 bytes, chunk index XOR (row mod 8).
-QFC_DEV uint32_t sw128_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
-
-// Work item i -> (query tile, head, sequence); heaviest (last) query tiles first.
-QFC_DEV void item_coords(int i, const Args& a, int& qt, int& h, int& b) {
-  const int per_tile = a.nq * a.B;
-  qt = a.q_tiles - 1 - i / per_tile;
-  const int r = i % per_tile;
+// Work item i -> (query tile pair, head, sequence); heaviest (last) pairs first.
+QFC_DEV void item_coords(int i, const Args& a, int& pr, int& h, int& b) {
+  const int per_pair = a.nq * a.B;
+  pr = a.q_pairs - 1 - i / per_pair;
+  const int r = i % per_pair;
   h = r % a.nq;
   b = r / a.nq;
 }
 
-// Persistent: each CTA walks work items blockIdx.x, +gridDim.x, ...  Every role walks
-// the same items, and a global tile counter t (over all items of this CTA) selects the
-// ring slot (t & 1) and mbarrier phase ((t >> 1) & 1) of every double buffer.
+// KV tiles of the pair's two query tiles (A = 2 pr, B = 2 pr + 1; B is empty past S).
+QFC_DEV void item_tiles(int pr, const Args& a, int kv_tiles, int& na, int& nb) {
+  const int qa = 2 * pr, qb = 2 * pr + 1;
+  na = min(qa + 1, kv_tiles);
+  nb = (qb < a.q_tiles) ? min(qb + 1, kv_tiles) : 0;
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + TILE_BYTES;          // 2 stages
-  uint8_t* sV = smem + 3 * TILE_BYTES;      // 2 stages
-  uint8_t* sP = smem + 5 * TILE_BYTES;      // 2 buffers
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * TILE_BYTES);
+  uint8_t* sQ = smem;                    // [2]: A, B
+  uint8_t* sK = smem + 2 * TILE_BYTES;   // [2] ring
+  uint8_t* sV = smem + 4 * TILE_BYTES;   // [2] ring
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * TILE_BYTES);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_empty = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;    // [2]
-  uint64_t* p_empty = bars + 11;  // [2]
-  uint64_t* o_full = bars + 13;   // [2]
-  uint64_t* o_empty = bars + 15;  // [2]
-  uint64_t* drain = bars + 17;
-  uint64_t* a_empty = bars + 18;  // [2] correction has read alpha / l of this buffer
-  uint64_t* q_empty = bars + 20;  // all QK MMAs of the current item are done with Q
-  uint64_t* v_full = bars + 21;   // [2] V^T tile landed (kv_full / kv_empty track K)
-  uint64_t* v_empty = bars + 23;  // [2] PV MMA done with V^T
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 25);
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;    // [2]
+  uint64_t* k_empty = bars + 4;   // [2]
+  uint64_t* v_full = bars + 6;    // [2]
+  uint64_t* v_empty = bars + 8;   // [2]
+  uint64_t* s_full = bars + 10;   // [2] per query tile
+  uint64_t* p_full = bars + 12;   // [2]
+  uint64_t* o_done = bars + 14;   // [2] the last issued PV of the tile is complete
+  uint64_t* o_empty = bars + 16;  // [2] the final O of the item has been read
+  uint64_t* drain = bars + 18;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* s_alpha = reinterpret_cast<float*>(tmem_holder + 4);  // [2][128]
-  float* s_l = s_alpha + 256;                                   // [2][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_items = args.q_tiles * args.nq * args.B;
+  const int n_items = args.q_pairs * args.nq * args.B;
   const int kv_tiles = (args.S + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
     tc::mbar_init(tc::smem_u32(q_full), 1);
     tc::mbar_init(tc::smem_u32(q_empty), 1);
     for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(tc::smem_u32(&kv_full[i]), 1);
-      tc::mbar_init(tc::smem_u32(&kv_empty[i]), 1);
-      tc::mbar_init(tc::smem_u32(&s_full[i]), 1);
-      tc::mbar_init(tc::smem_u32(&s_empty[i]), 128);
-      tc::mbar_init(tc::smem_u32(&p_full[i]), 128);
-      tc::mbar_init(tc::smem_u32(&p_empty[i]), 1);
-      tc::mbar_init(tc::smem_u32(&o_full[i]), 1);
-      tc::mbar_init(tc::smem_u32(&o_empty[i]), 128);
-      tc::mbar_init(tc::smem_u32(&a_empty[i]), 128);
+      tc::mbar_init(tc::smem_u32(&k_full[i]), 1);
+      tc::mbar_init(tc::smem_u32(&k_empty[i]), 1);
       tc::mbar_init(tc::smem_u32(&v_full[i]), 1);
       tc::mbar_init(tc::smem_u32(&v_empty[i]), 1);
+      tc::mbar_init(tc::smem_u32(&s_full[i]), 1);
+      tc::mbar_init(tc::smem_u32(&p_full[i]), 128);
+      tc::mbar_init(tc::smem_u32(&o_done[i]), 1);
+      tc::mbar_init(tc::smem_u32(&o_empty[i]), 128);
     }
     tc::mbar_init(tc::smem_u32(drain), 1);
     *s_abort = 0;
@@ -139,7 +142,7 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) 
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
-  const uint32_t tmem = *tmem_holder;  // S[0]=+0, S[1]=+128, O[0]=+256, O[1]=+384
+  const uint32_t tmem = *tmem_holder;  // S_A = +0, S_B = +128, O_A = +256, O_B = +384
   auto wait = [&](uint64_t* bar, uint32_t parity) {
     return tc::mbar_wait(tc::smem_u32(bar), parity, globaltimer_ns() + args.timeout_ns, s_abort);
   };
@@ -148,57 +151,59 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) 
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       tc::tma_prefetch_desc(&tmQKV);
-      int t = 0, k = 0;
-      int issued[2] = {-1, -1}, v_issued[2] = {-1, -1}, q_issued = -1;
+      int tk = 0, k = 0;  // KV tiles loaded (all items), items started
+      int k_issued[2] = {-1, -1}, v_issued[2] = {-1, -1}, q_issued = -1;
       bool ok = true;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++k) {
-        int qt, h, b;
-        item_coords(item, args, qt, h, b);
+        int pr, h, b, na, nb;
+        item_coords(item, args, pr, h, b);
+        item_tiles(pr, args, kv_tiles, na, nb);
+        const int n_kv = max(na, nb);
         const int kvh = h / args.group;
         const int row_base = b * args.S;
-        const int n_kv = min(qt + 1, kv_tiles);
         if (!wait(q_empty, (k & 1) ^ 1)) {
-          fail(args, s_abort, 0x1002);
+          fail(args, s_abort, 0x1001);
           break;
         }
         const uint32_t qb = tc::smem_u32(q_full);
-        tc::mbar_arrive_expect_tx(qb, TILE_BYTES);
-        tc::tma_load_2d(tc::smem_u32(sQ), &tmQKV, qb, h * HD, row_base + qt * BQ);
-        tc::tma_load_2d(tc::smem_u32(sQ + HALF_BYTES), &tmQKV, qb, h * HD + 64, row_base + qt * BQ);
+        tc::mbar_arrive_expect_tx(qb, 2 * TILE_BYTES);
+        for (int t = 0; t < 2; ++t) {  // rows past the batch's end read as zero; unused rows are masked
+          const int qrow = row_base + (2 * pr + t) * BQ;
+          tc::tma_load_2d(tc::smem_u32(sQ + t * TILE_BYTES), &tmQKV, qb, h * HD, qrow);
+          tc::tma_load_2d(tc::smem_u32(sQ + t * TILE_BYTES + HALF_BYTES), &tmQKV, qb, h * HD + 64, qrow);
+        }
         q_issued = k;
-        for (int j = 0; j < n_kv; ++j, ++t) {
-          const int st = t & 1;
-          if (!wait(&kv_empty[st], ((t >> 1) & 1) ^ 1)) {
-            fail(args, s_abort, 0x1001);
+        const int kcol = (args.nq + kvh) * HD, vcol = (args.nq + args.nkv + kvh) * HD;
+        for (int j = 0; j < n_kv; ++j, ++tk) {
+          const int st = tk & 1;
+          if (!wait(&k_empty[st], ((tk >> 1) & 1) ^ 1)) {
+            fail(args, s_abort, 0x1002);
             ok = false;
             break;
           }
-          const uint32_t fb = tc::smem_u32(&kv_full[st]);
+          const uint32_t fb = tc::smem_u32(&k_full[st]);
           tc::mbar_arrive_expect_tx(fb, TILE_BYTES);
-          const int kcol = (args.nq + kvh) * HD;
           tc::tma_load_2d(tc::smem_u32(sK + st * TILE_BYTES), &tmQKV, fb, kcol, row_base + j * BKV);
           tc::tma_load_2d(tc::smem_u32(sK + st * TILE_BYTES + HALF_BYTES), &tmQKV, fb, kcol + 64, row_base + j * BKV);
-          issued[st] = t;
-          // V^T of this tile: its slot frees later (after PV), so it is loaded second
-          if (!wait(&v_empty[st], ((t >> 1) & 1) ^ 1)) {
+          k_issued[st] = tk;
+          if (!wait(&v_empty[st], ((tk >> 1) & 1) ^ 1)) {
             fail(args, s_abort, 0x1003);
             ok = false;
             break;
           }
           const uint32_t vb = tc::smem_u32(&v_full[st]);
           tc::mbar_arrive_expect_tx(vb, TILE_BYTES);
-          const int vcol = (args.nq + args.nkv + kvh) * HD;
           tc::tma_load_2d(tc::smem_u32(sV + st * TILE_BYTES), &tmQKV, vb, vcol, row_base + j * BKV);
           tc::tma_load_2d(tc::smem_u32(sV + st * TILE_BYTES + HALF_BYTES), &tmQKV, vb, vcol + 64, row_base + j * BKV);
-          v_issued[st] = t;
+          v_issued[st] = tk;
         }
       }
       if (*s_abort) {  // let issued copies land before shared memory goes away
         int never = 0;
         if (q_issued >= 0) tc::mbar_wait(tc::smem_u32(q_full), q_issued & 1, globaltimer_ns() + 50000000ull, &never);
         for (int st = 0; st < 2; ++st) {
-          if (issued[st] >= 0)
-            tc::mbar_wait(tc::smem_u32(&kv_full[st]), (issued[st] >> 1) & 1, globaltimer_ns() + 50000000ull, &never);
+          if (k_issued[st] >= 0)
+            tc::mbar_wait(tc::smem_u32(&k_full[st]), (k_issued[st] >> 1) & 1, globaltimer_ns() + 50000000ull, &never);
           if (v_issued[st] >= 0)
             tc::mbar_wait(tc::smem_u32(&v_full[st]), (v_issued[st] >> 1) & 1, globaltimer_ns() + 50000000ull, &never);
         }
@@ -208,61 +213,84 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) 
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       bool ok = true, issued_any = false;
-      int t = 0, k = 0;
-      auto issue_qk = [&](int tt) -> bool {
-        const int st = tt & 1;
-        if (!wait(&kv_full[st], (tt >> 1) & 1) || !wait(&s_empty[st], ((tt >> 1) & 1) ^ 1)) return false;
+      int tk = 0, k = 0;
+      int ns[2] = {0, 0};  // S MMAs issued per query tile (all items)
+      int np[2] = {0, 0};  // PV MMAs issued per query tile
+      int ni[2] = {0, 0};  // items started per query tile
+      // S_t = Q_t K^T for the KV tile with counter j_tk.  Its columns held P_t of the previous
+      // tile, whose PV was issued before: the in-order tensor pipe reads P first.
+      auto issue_s = [&](int t, int j_tk) -> bool {
         tc::tc_fence_after();
-        const uint32_t a0 = tc::smem_u32(sQ), b0 = tc::smem_u32(sK + st * TILE_BYTES);
+        const uint32_t a0 = tc::smem_u32(sQ + t * TILE_BYTES), b0 = tc::smem_u32(sK + (j_tk & 1) * TILE_BYTES);
 #pragma unroll
         for (int s = 0; s < 2; ++s)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            tc::umma_f16(tmem + st * 128, tc::sw128_kmajor_desc(a0 + s * HALF_BYTES + kk * 32),
+            tc::umma_f16(tmem + t * 128, tc::sw128_kmajor_desc(a0 + s * HALF_BYTES + kk * 32),
                          tc::sw128_kmajor_desc(b0 + s * HALF_BYTES + kk * 32), IDESC, (s | kk) != 0);
-        tc::umma_commit(tc::smem_u32(&s_full[st]));
-        tc::umma_commit(tc::smem_u32(&kv_empty[st]));  // K slot free once this QK is done
+        tc::umma_commit(tc::smem_u32(&s_full[t]));
+        ++ns[t];
+        issued_any = true;
+        return true;
+      };
+      auto issue_pv = [&](int t, bool first, int v_tk) -> bool {  // O_t (+)= P_t V
+        if (!wait(&p_full[t], np[t] & 1)) return false;
+        if (first && !wait(&o_empty[t], (ni[t] & 1) ^ 1)) return false;
+        tc::tc_fence_after();
+        const uint32_t b0 = tc::smem_u32(sV + (v_tk & 1) * TILE_BYTES);
+        // P: TMEM columns t*128 + 8 i hold keys 16 i .. 16 i + 15.  V: MN-major as loaded
+        // (rows = keys, 64 head dims per 128-byte row, the second 64 dims HALF_BYTES later);
+        // 16 keys = 2048 bytes per MMA.
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          tc::umma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + i * 8,
+                          tc::sw128_mnmajor_desc(b0 + i * 2048, HALF_BYTES), IDESC_PV, !first || i != 0);
+        tc::umma_commit(tc::smem_u32(&o_done[t]));
+        ++np[t];
+        if (first) ++ni[t];
         issued_any = true;
         return true;
       };
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++k) {
-        int qt, h, b;
-        item_coords(item, args, qt, h, b);
-        const int n_kv = min(qt + 1, kv_tiles);
-        if (!wait(q_full, k & 1) || !issue_qk(t)) {
+        int pr, h, b, na, nb;
+        item_coords(item, args, pr, h, b);
+        item_tiles(pr, args, kv_tiles, na, nb);
+        const int n_kv = max(na, nb);
+        const int nt[2] = {na, nb};
+        if (!wait(q_full, k & 1) || !wait(&k_full[tk & 1], (tk >> 1) & 1)) {
           ok = false;
           break;
         }
-        for (int j = 0; j < n_kv; ++j, ++t) {
-          const int st = t & 1;
-          if (j + 1 < n_kv) {
-            if (!issue_qk(t + 1)) {
-              ok = false;
-              break;
-            }
-          } else {
-            tc::umma_commit(tc::smem_u32(q_empty));  // Q free once this item's QK MMAs are done
-          }
-          if (!wait(&p_full[st], (t >> 1) & 1) || !wait(&o_empty[st], ((t >> 1) & 1) ^ 1) ||
-              !wait(&v_full[st], (t >> 1) & 1)) {
+        // prologue: S of KV tile 0 for both query tiles
+        for (int t = 0; t < 2 && ok; ++t)
+          if (nt[t] > 0 && !issue_s(t, tk)) ok = false;
+        if (!ok) break;
+        tc::umma_commit(tc::smem_u32(&k_empty[tk & 1]));
+        if (n_kv == 1) tc::umma_commit(tc::smem_u32(q_empty));
+        for (int j = 0; j < n_kv && ok; ++j) {
+          const int cur = tk + j;
+          const bool more = j + 1 < n_kv;
+          if (!wait(&v_full[cur & 1], (cur >> 1) & 1)) {
             ok = false;
             break;
           }
-          tc::tc_fence_after();
-          const uint32_t a0 = tc::smem_u32(sP + st * TILE_BYTES), b0 = tc::smem_u32(sV + st * TILE_BYTES);
-          // P: K-major, keys split in two 64-key swizzle tiles.  V: MN-major as loaded
-          // (rows = keys, 64 head dims per 128-byte row, second 64 dims HALF_BYTES later);
-          // 16 keys = 2048 bytes per MMA.
-#pragma unroll
-          for (int s = 0; s < 2; ++s)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              tc::umma_f16(tmem + 256 + st * 128, tc::sw128_kmajor_desc(a0 + s * HALF_BYTES + kk * 32),
-                           tc::sw128_mnmajor_desc(b0 + (s * 4 + kk) * 2048, HALF_BYTES), IDESC_PV, (s | kk) != 0);
-          tc::umma_commit(tc::smem_u32(&o_full[st]));
-          tc::umma_commit(tc::smem_u32(&p_empty[st]));
-          tc::umma_commit(tc::smem_u32(&v_empty[st]));
+          bool k_ready = false;  // K_{j+1} is waited for only right before its first use
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j < nt[t] && !issue_pv(t, j == 0, cur)) ok = false;
+            if (ok && more && j + 1 < nt[t]) {
+              if (!k_ready && !wait(&k_full[(cur + 1) & 1], ((cur + 1) >> 1) & 1)) ok = false;
+              k_ready = true;
+              if (ok && !issue_s(t, cur + 1)) ok = false;
+            }
+          }
+          if (!ok) break;
+          tc::umma_commit(tc::smem_u32(&v_empty[cur & 1]));  // V free once both PV MMAs are done
+          if (more) {
+            tc::umma_commit(tc::smem_u32(&k_empty[(cur + 1) & 1]));
+            if (j + 2 == n_kv) tc::umma_commit(tc::smem_u32(q_empty));  // the item's last S MMAs
+          }
         }
+        tk += n_kv;
       }
       if (!ok) fail(args, s_abort, 0x2001);
       if ((!ok || *s_abort) && issued_any) {
@@ -271,21 +299,24 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) 
         tc::mbar_wait(tc::smem_u32(drain), 0, globaltimer_ns() + 50000000ull, &never);
       }
     }
-  } else if (warp < 6) {
-    // ---------------------------------------------------------------- softmax
-    const int r = (warp & 3) * 32 + lane;  // query row in the tile (= TMEM lane)
+  } else {
+    // ---------------------------------------------------------------- softmax (tile A or B)
+    const int t = (warp - 2) >> 2;             // 0: query tile A (warps 2-5), 1: B (warps 6-9)
+    const int r = (warp & 3) * 32 + lane;      // query row in the tile (= TMEM lane)
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    int t = 0;
+    const uint32_t s_col = tmem + lane_off + t * 128, o_col = tmem + lane_off + 256 + t * 128;
+    int n = 0;  // tiles processed by this query tile (all items)
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      int qt, h, b;
-      item_coords(item, args, qt, h, b);
-      const int n_kv = min(qt + 1, kv_tiles);
-      const int qpos = qt * BQ + r;
-      float m = -INFINITY, l = 0.f;
-      for (int j = 0; j < n_kv; ++j, ++t) {
-        const int st = t & 1;
-        if (!wait(&s_full[st], (t >> 1) & 1)) {
+      int pr, h, b, na, nb;
+      item_coords(item, args, pr, h, b);
+      item_tiles(pr, args, kv_tiles, na, nb);
+      const int my_n = t == 0 ? na : nb;
+      if (my_n == 0) continue;
+      const int qpos = (2 * pr + t) * BQ + r;
+      float m_ref = -INFINITY, l = 0.f;
+      for (int j = 0; j < my_n; ++j, ++n) {
+        if (!wait(&s_full[t], n & 1)) {
           fail(args, s_abort, 0x3001);
           ok = false;
           break;
@@ -295,7 +326,7 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) 
         {
           uint32_t u[4][32];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) tc::tmem_ld_32x32b_x32(tmem + st * 128 + lane_off + c * 32, u[c]);
+          for (int c = 0; c < 4; ++c) tc::tmem_ld_32x32b_x32(s_col + c * 32, u[c]);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -304,8 +335,6 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) 
             for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[c][i]);
           }
         }
-        tc::tc_fence_before();
-        tc::mbar_arrive(tc::smem_u32(&s_empty[st]));
         // columns past kmax are masked: keys above the diagonal or past the sequence end
         const int kmax = min(qpos, args.S - 1) - j * BKV;
         if (kmax < BKV - 1) {
@@ -319,95 +348,76 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) 
           for (int q = 0; q < 4; ++q) mx4[q] = fmaxf(mx4[q], sv[i + q]);
         }
         const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * args.scale_log2;
-        const float m_new = fmaxf(m, mx);
-        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        const float alpha = ex2(m - m_use);
-        // P buffer st is free once PV(t-2) finished reading it
-        if (!wait(&p_empty[st], ((t >> 1) & 1) ^ 1)) {
-          fail(args, s_abort, 0x3002);
-          ok = false;
-          break;
+        // S of this tile completed after the previous PV of this tile (in-order tensor pipe),
+        // so O holds every earlier tile and may be rescaled here.
+        float alpha = 1.f;
+        if (j == 0 || mx > m_ref + kRescaleLog2) {
+          const float m_new = fmaxf(m_ref, mx);
+          const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+          if (j > 0) {
+            alpha = ex2(m_ref - m_use);
+            // O row *= alpha, in TMEM
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t u[32];
+              tc::tmem_ld_32x32b_x32(o_col + c * 32, u);
+              tc::tmem_wait_ld();
+              tc::tmem_reg_fence(u);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
+              tc::tmem_st_32x32b_x32(o_col + c * 32, u);
+            }
+            tc::tmem_wait_st();
+          }
+          m_ref = m_use;
         }
         float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-        uint8_t* pbase = sP + st * TILE_BYTES;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 keys
-          uint32_t w[4];
+        for (int c = 0; c < 4; ++c) {  // 4 chunks of 32 keys -> 16 TMEM columns of bf16 pairs
+          uint32_t w[16];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float p0 = ex2(fmaf(sv[c * 8 + 2 * q], args.scale_log2, -m_use));
-            const float p1 = ex2(fmaf(sv[c * 8 + 2 * q + 1], args.scale_log2, -m_use));
-            sum4[q] += p0 + p1;
-            w[q] = pack_bf16x2(p0, p1);
+          for (int q = 0; q < 16; ++q) {
+            const float p0 = ex2(fmaf(sv[c * 32 + 2 * q], args.scale_log2, -m_ref));
+            const float p1 = ex2(fmaf(sv[c * 32 + 2 * q + 1], args.scale_log2, -m_ref));
+            sum4[q & 3] += p0 + p1;
+            w[q] = pack_bf16x2(p0, p1);  // key 2q in the low half
           }
-          uint8_t* dst = pbase + (c >> 3) * HALF_BYTES + sw128_off(r, c & 7);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+          tc::tmem_st_32x32b_x16(s_col + c * 16, w);
         }
-        fence_async_smem();
-        // alpha / l buffer st is free once the correction thread has read tile t-2's
-        if (!wait(&a_empty[st], ((t >> 1) & 1) ^ 1)) {
-          fail(args, s_abort, 0x3003);
-          ok = false;
-          break;
-        }
-        l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-        m = m_new;
-        s_alpha[st * 128 + r] = alpha;
-        s_l[st * 128 + r] = l;
-        tc::mbar_arrive(tc::smem_u32(&p_full[st]));
-      }
-    }
-  } else {
-    // ---------------------------------------------------------------- correction / output
-    const int r = (warp & 3) * 32 + lane;
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    int t = 0;
-    bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      int qt, h, b;
-      item_coords(item, args, qt, h, b);
-      const int n_kv = min(qt + 1, kv_tiles);
-      float o[HD];
-#pragma unroll
-      for (int i = 0; i < HD; ++i) o[i] = 0.f;
-      float l_final = 1.f;
-      for (int j = 0; j < n_kv; ++j, ++t) {
-        const int st = t & 1;
-        if (!wait(&p_full[st], (t >> 1) & 1) || !wait(&o_full[st], (t >> 1) & 1)) {
-          fail(args, s_abort, 0x4001);
-          ok = false;
-          break;
-        }
-        tc::tc_fence_after();
-        const float alpha = s_alpha[st * 128 + r];
-        l_final = s_l[st * 128 + r];
-        tc::mbar_arrive(tc::smem_u32(&a_empty[st]));
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t u[32];
-          tc::tmem_ld_32x32b_x32(tmem + 256 + st * 128 + lane_off + c * 32, u);
-          tc::tmem_wait_ld();
-          tc::tmem_reg_fence(u);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha, __uint_as_float(u[i]));
-        }
+        tc::tmem_wait_st();
         tc::tc_fence_before();
-        tc::mbar_arrive(tc::smem_u32(&o_empty[st]));
+        l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+        tc::mbar_arrive(tc::smem_u32(&p_full[t]));
       }
-      // l_final was written by this row's softmax thread before its last p_full arrival
-      if (!ok || *s_abort) break;
-      const int qpos = qt * BQ + r;
+      if (!ok) break;
+      // the item's last PV is done: O / l to global memory, then O's columns are free
+      if (!wait(&o_done[t], (n - 1) & 1)) {
+        fail(args, s_abort, 0x3003);
+        break;
+      }
+      tc::tc_fence_after();
+      uint32_t u[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld_32x32b_x32(o_col + c * 32, u[c]);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_reg_fence(u[c]);
+      tc::tc_fence_before();
+      tc::mbar_arrive(tc::smem_u32(&o_empty[t]));
       if (qpos < args.S) {
-        const float inv = 1.f / l_final;
+        const float inv = 1.f / l;
         __nv_bfloat16* dst = args.out + (int64_t)(b * args.S + qpos) * (args.nq * HD) + h * HD;
 #pragma unroll
-        for (int c = 0; c < HD / 8; ++c) {
-          const uint4 v = make_uint4(pack_bf16x2(o[8 * c] * inv, o[8 * c + 1] * inv),
-                                     pack_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
-                                     pack_bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv),
-                                     pack_bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
-          reinterpret_cast<uint4*>(dst)[c] = v;
-        }
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t* x = &u[c][8 * q];
+            const uint4 v = make_uint4(pack_bf16x2(__uint_as_float(x[0]) * inv, __uint_as_float(x[1]) * inv),
+                                       pack_bf16x2(__uint_as_float(x[2]) * inv, __uint_as_float(x[3]) * inv),
+                                       pack_bf16x2(__uint_as_float(x[4]) * inv, __uint_as_float(x[5]) * inv),
+                                       pack_bf16x2(__uint_as_float(x[6]) * inv, __uint_as_float(x[7]) * inv));
+            reinterpret_cast<uint4*>(dst)[c * 4 + q] = v;
+          }
       }
     }
   }
@@ -486,13 +496,14 @@ void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_
   a.nkv = (int)nkv;
   a.group = (int)(nq / nkv);
   a.q_tiles = (int)((S + BQ - 1) / BQ);
+  a.q_pairs = (a.q_tiles + 1) / 2;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.status = status_word();
   a.timeout_ns = 10000000000ull;
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t items = (int64_t)a.q_tiles * nq * B;
+  const int64_t items = (int64_t)a.q_pairs * nq * B;
   const int grid = (int)std::min<int64_t>(items, sms);
   attn_prefill_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tq, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -347,6 +347,99 @@ QFC_DEV void group_minmax16(const uint4& r, int lpg, float& mn, float& mx) {
 }
 
 // ------------------------------------------------------------------------------------
+// 16 elements per lane (a 512-element warp unit): vector I/O and group statistics
+// ------------------------------------------------------------------------------------
+constexpr int kEPL = 16;
+constexpr int kUnit16 = 32 * kEPL;  // elements per warp unit
+
+// 16 consecutive 16-bit elements as two 16-byte vectors; elements at or beyond n read 0.
+struct Raw16 {
+  uint4 a, b;
+};
+template <typename T>
+QFC_DEV Raw16 load_raw16(const T* base, int64_t idx, int64_t n) {
+  Raw16 r;
+  if (idx + kEPL <= n) {
+    const uint4* p = reinterpret_cast<const uint4*>(base + idx);
+    r.a = p[0];
+    r.b = p[1];
+  } else {
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(base);
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t lo = (idx + 2 * i < n) ? h[idx + 2 * i] : 0u;
+      const uint32_t hi = (idx + 2 * i + 1 < n) ? h[idx + 2 * i + 1] : 0u;
+      w[i] = lo | (hi << 16);
+    }
+    r.a = make_uint4(w[0], w[1], w[2], w[3]);
+    r.b = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+  return r;
+}
+template <typename T>
+QFC_DEV void raw16_to_f32(const Raw16& r, float (&v)[16]) {
+  const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) unpack_bf16x2(w[i], v[2 * i], v[2 * i + 1]);
+    else unpack_f16x2(w[i], v[2 * i], v[2 * i + 1]);
+  }
+}
+template <typename T>
+QFC_DEV void store16_guard(T* base, int64_t idx, int64_t n, const float (&v)[16]) {
+  if (idx + kEPL <= n) {
+    uint4* d = reinterpret_cast<uint4*>(base + idx);
+    const float(&lo)[8] = *reinterpret_cast<const float(*)[8]>(&v[0]);
+    const float(&hi)[8] = *reinterpret_cast<const float(*)[8]>(&v[8]);
+    d[0] = Vec8IO<T>::pack(lo);
+    d[1] = Vec8IO<T>::pack(hi);
+  } else {
+#pragma unroll
+    for (int i = 0; i < kEPL; ++i)
+      if (idx + i < n) base[idx + i] = from_f32<T>(v[i]);
+  }
+}
+
+// Group (min, max) of 16-bit inputs: the lane's 16 values reduce as packed pairs, then
+// the (-min, max) pair crosses lpg lanes as one word per shuffle level.  Exact.
+template <typename T>
+QFC_DEV void group_minmax16x16(const Raw16& r, int lpg, float& mn, float& mx) {
+  using T2 = typename std::conditional<std::is_same<T, __nv_bfloat16>::value, __nv_bfloat162, __half2>::type;
+  auto as2 = [](uint32_t u) { return *reinterpret_cast<T2*>(&u); };
+  auto bits = [](T2 x) { return *reinterpret_cast<uint32_t*>(&x); };
+  const T2 hi = __hmax2(__hmax2(__hmax2(as2(r.a.x), as2(r.a.y)), __hmax2(as2(r.a.z), as2(r.a.w))),
+                        __hmax2(__hmax2(as2(r.b.x), as2(r.b.y)), __hmax2(as2(r.b.z), as2(r.b.w))));
+  const T2 lo = __hmin2(__hmin2(__hmin2(as2(r.a.x), as2(r.a.y)), __hmin2(as2(r.a.z), as2(r.a.w))),
+                        __hmin2(__hmin2(as2(r.b.x), as2(r.b.y)), __hmin2(as2(r.b.z), as2(r.b.w))));
+  const uint32_t nlo = bits(lo) ^ 0x80008000u;             // (-min_even, -min_odd)
+  const uint32_t q1 = __byte_perm(nlo, bits(hi), 0x7610);  // (-min_even, max_odd)
+  const uint32_t q2 = __byte_perm(nlo, bits(hi), 0x5432);  // (-min_odd,  max_even)
+  uint32_t p = bits(__hmax2(as2(q1), as2(q2)));            // (-min, max)
+  for (int off = lpg >> 1; off > 0; off >>= 1) p = bits(__hmax2(as2(p), as2(__shfl_xor_sync(QFC_FULL_MASK, p, off))));
+  float a, b;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) unpack_bf16x2(p, a, b);
+  else unpack_f16x2(p, a, b);
+  mn = -a;
+  mx = b;
+}
+// Same for fp32 values (the reduced sum in phase 2).
+QFC_DEV void group_minmax_f32x16(const float (&v)[16], int lpg, float& mn, float& mx) {
+  float a[4], b[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    a[q] = fminf(fminf(v[q], v[q + 4]), fminf(v[q + 8], v[q + 12]));
+    b[q] = fmaxf(fmaxf(v[q], v[q + 4]), fmaxf(v[q + 8], v[q + 12]));
+  }
+  mn = fminf(fminf(a[0], a[1]), fminf(a[2], a[3]));
+  mx = fmaxf(fmaxf(b[0], b[1]), fmaxf(b[2], b[3]));
+  for (int off = lpg >> 1; off > 0; off >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(QFC_FULL_MASK, mn, off));
+    mx = fmaxf(mx, __shfl_xor_sync(QFC_FULL_MASK, mx, off));
+  }
+}
+
+// ------------------------------------------------------------------------------------
 // Rotary embedding of one (x1, x2) pair (elements i and i + hd/2 of a head) with the
 // position's (cos, sin): the rounding is spelled out so that the standalone RoPE kernel
 // and the GEMM epilogue that fuses it give identical bits.

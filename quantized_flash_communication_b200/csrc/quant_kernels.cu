@@ -126,6 +126,60 @@ quantize_kernel(const T* __restrict__ x, uint8_t* __restrict__ q, ST* __restrict
   }
 }
 
+// 16-bit inputs, group sizes 16..256: a warp unit is 512 elements, 16 per lane (two
+// 16-byte loads, one 16-byte store of codes), so the per-lane address, guard and group-
+// parameter work is spread over twice the elements of the 8-per-lane kernel; the lane's
+// 16 values reduce their (-min, max) pair as packed 16-bit values before the shuffles.
+// Same codes and parameters bit for bit.
+template <typename T, int BITS, bool SYM, typename ST>
+__global__ void __launch_bounds__(kThreads)
+quantize16_kernel(const T* __restrict__ x, uint8_t* __restrict__ q, ST* __restrict__ s_out,
+                  __half* __restrict__ z_out, int64_t n, int gs_shift) {
+  using QM = QMath<BITS, SYM>;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int lpg = 1 << (gs_shift - 4);  // lanes per group
+  const bool leader = (lane & (lpg - 1)) == 0;
+  const int64_t n_units = (n + kUnit16 - 1) / kUnit16;
+  constexpr int kUnroll = 2;  // independent 32-byte loads in flight per lane
+  for (int64_t ub = warp; ub < n_units; ub += kUnroll * nwarps) {
+    Raw16 raws[kUnroll];
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k)
+      if (ub + k * nwarps < n_units) raws[k] = load_raw16(x, (ub + k * nwarps) * kUnit16 + lane * kEPL, n);
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const int64_t u = ub + k * nwarps;
+      if (u >= n_units) break;
+      const int64_t idx = u * kUnit16 + lane * kEPL;
+      float mn, mx;
+      group_minmax16x16<T>(raws[k], lpg, mn, mx);
+      float v[16];
+      raw16_to_f32<T>(raws[k], v);
+      float s, inv, z;
+      QM::params(mn, mx, s, inv, z);
+      uint32_t m[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) m[i] = QM::codebits(v[i], inv, z);
+      const uint32_t(&m_lo)[8] = *reinterpret_cast<const uint32_t(*)[8]>(&m[0]);
+      const uint32_t(&m_hi)[8] = *reinterpret_cast<const uint32_t(*)[8]>(&m[8]);
+      const uint2 a = codebits8_to_u2(m_lo), b = codebits8_to_u2(m_hi);
+      if (idx + kEPL <= n) {
+        *reinterpret_cast<uint4*>(q + idx) = make_uint4(a.x, a.y, b.x, b.y);
+      } else {
+        for (int i = 0; i < kEPL; ++i)
+          if (idx + i < n) q[idx + i] = (uint8_t)(m[i] & 0xffu);
+      }
+      if (leader && idx < n) {
+        const int64_t g = idx >> gs_shift;
+        store_scale<ST>(s_out + g, s);
+        z_out[g] = __float2half_rn(z);
+      }
+    }
+  }
+}
+
 // Codes may arrive as bytes or as fp16 values (the unpacker's output, as in the reference
 // where triton_dequantize consumes unpack_int4's fp16 codes, communication.py:55-59).
 template <typename QT> struct CodeLoad;
@@ -248,12 +302,26 @@ template <typename T, typename ST>
 void launch_quantize_t(const at::Tensor& x, at::Tensor& q, at::Tensor& s, at::Tensor& z, int bits,
                        bool sym, int gs, cudaStream_t st) {
   const int64_t n = x.numel();
-  const int64_t warps = gs <= 256 ? (n + 255) / 256 : (n + gs - 1) / gs;
-  const int grid = grid_for_warps(warps);
   const T* xp = reinterpret_cast<const T*>(x.data_ptr());
   uint8_t* qp = reinterpret_cast<uint8_t*>(q.data_ptr());
   ST* sp = reinterpret_cast<ST*>(s.data_ptr());
   __half* zp = reinterpret_cast<__half*>(z.data_ptr());
+  if constexpr (sizeof(T) == 2) {
+    if (gs >= 16 && gs <= 256) {
+      const int grid16 = grid_for_warps((n + kUnit16 - 1) / kUnit16);
+      const int gsh = __builtin_ctz((unsigned)gs);
+#define QFC_LAUNCH_Q16(B, S) quantize16_kernel<T, B, S, ST><<<grid16, kThreads, 0, st>>>(xp, qp, sp, zp, n, gsh)
+      if (bits == 8 && !sym) QFC_LAUNCH_Q16(8, false);
+      else if (bits == 8 && sym) QFC_LAUNCH_Q16(8, true);
+      else if (bits == 4 && !sym) QFC_LAUNCH_Q16(4, false);
+      else QFC_LAUNCH_Q16(4, true);
+#undef QFC_LAUNCH_Q16
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      return;
+    }
+  }
+  const int64_t warps = gs <= 256 ? (n + 255) / 256 : (n + gs - 1) / gs;
+  const int grid = grid_for_warps(warps);
 #define QFC_LAUNCH_Q(B, S) quantize_kernel<T, B, S, ST><<<grid, kThreads, 0, st>>>(xp, qp, sp, zp, n, gs)
   if (bits == 8 && !sym) QFC_LAUNCH_Q(8, false);
   else if (bits == 8 && sym) QFC_LAUNCH_Q(8, true);

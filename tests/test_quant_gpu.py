@@ -11,7 +11,7 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("mode", ["asym", "sym"])
-@pytest.mark.parametrize("gs", [8, 32, 64, 128, 256, 1024, 8192])
+@pytest.mark.parametrize("gs", [8, 16, 32, 64, 128, 256, 1024, 8192])
 def test_quantize_bit_exact(cuda_device, dtype, bits, mode, gs):
     torch.manual_seed(gs + bits)
     for n in (1, 9, 255, 4096, 100003):
