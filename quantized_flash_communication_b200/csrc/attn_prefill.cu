@@ -55,6 +55,9 @@ constexpr uint32_t IDESC_PV = tc::idesc_f16(128, 128, true, true);  // O = P V, 
 constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 2048;
 // log2-domain growth of the row maximum tolerated before O is rescaled (P <= 2^8)
 constexpr float kRescaleLog2 = 8.f;
+// Every kPolyEvery-th pair of exponentials is evaluated on the FMA pipe (0: none), which
+// balances the MUFU unit against the FMA pipe's other softmax work.
+constexpr int kPolyEvery = 4;
 
 struct Args {
   int B, S, nq, nkv, group;
@@ -74,6 +77,28 @@ QFC_DEV float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x for x <= 0 on the FMA pipe, to share the softmax's exponentials with the MUFU unit.
+// Range reduction to x = i + f with i = round(x), f in [-1/2, 1/2]: adding 1.5 * 2^23
+// leaves i in the low mantissa bits of r (round to nearest), then 2^f is a cubic whose
+// coefficients were fitted for this library to minimise the maximum relative error on
+// [-1/2, 1/2] (Lawson's iteratively reweighted least squares, a standard route to the
+// minimax polynomial); that error is 7.5e-5, far below the 2^-9 half-ulp of the bf16 P it
+// feeds.  2^i enters by adding i to the exponent field.  x is clamped at -125, so masked
+// scores (-inf) give 2^-125 instead of 0, which no bf16 sum can see.
+constexpr float kEx2C0 = 0.99992812f, kEx2C1 = 0.69326097f, kEx2C2 = 0.24261054f, kEx2C3 = 0.05517132f;
+QFC_DEV float ex2_poly(float x) {
+  x = fmaxf(x, -125.f);
+  const float r = x + 12582912.f;  // 1.5 * 2^23
+  const float f = x - (r - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(kEx2C3, f, kEx2C2), f, kEx2C1), f, kEx2C0);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(r) << 23));
+}
+
+__global__ void exp2_poly_kernel(const float* x, float* y, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = ex2_poly(x[i]);
 }
 
 // Work item i -> (query tile pair, head, sequence); heaviest (last) pairs first.
@@ -377,8 +402,12 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) 
           uint32_t w[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const float p0 = ex2(fmaf(sv[c * 32 + 2 * q], args.scale_log2, -m_ref));
-            const float p1 = ex2(fmaf(sv[c * 32 + 2 * q + 1], args.scale_log2, -m_ref));
+            // one pair in kPolyEvery on the FMA pipe, the rest on MUFU
+            const float a0 = fmaf(sv[c * 32 + 2 * q], args.scale_log2, -m_ref);
+            const float a1 = fmaf(sv[c * 32 + 2 * q + 1], args.scale_log2, -m_ref);
+            const bool poly = kPolyEvery > 0 && (q % kPolyEvery) == kPolyEvery - 1;
+            const float p0 = poly ? ex2_poly(a0) : ex2(a0);
+            const float p1 = poly ? ex2_poly(a1) : ex2(a1);
             sum4[q & 3] += p0 + p1;
             w[q] = pack_bf16x2(p0, p1);  // key 2q in the low half
           }
@@ -506,6 +535,19 @@ void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_
   const int64_t items = (int64_t)a.q_pairs * nq * B;
   const int grid = (int)std::min<int64_t>(items, sms);
   attn_prefill_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tq, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// y = 2^x through the softmax's FMA-pipe exponential (for tests against exp2f).
+void attn_exp2_poly(const at::Tensor& x, at::Tensor& y) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous() && y.sizes() == x.sizes() &&
+                  y.scalar_type() == at::kFloat && y.is_contiguous(), "attn_exp2_poly: fp32 CUDA tensors");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t n = x.numel();
+  if (n == 0) return;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
+  attn::exp2_poly_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(x.data_ptr<float>(),
+                                                                               y.data_ptr<float>(), n);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

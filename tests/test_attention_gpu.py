@@ -31,3 +31,19 @@ def test_prefill_attention_matches_reference(cuda_device, B, S, nq, nkv):
     ref = _ref(qkv, B, S, nq, nkv, hd)
     assert rel_l2(o.float(), ref) < 1e-2
     assert torch.isfinite(o.float()).all()
+
+
+def test_fma_pipe_exp2_against_exp2f(cuda_device):
+    """The softmax's polynomial 2^x (FMA pipe) vs CUDA's exp2f (torch.exp2) on x <= 0."""
+    from quantized_flash_communication_b200._ext import ext
+    x = torch.cat([torch.linspace(-125.0, 0.0, 1 << 20, device=cuda_device),
+                   -torch.rand(1 << 20, device=cuda_device) * 30,
+                   torch.tensor([0.0, -0.5, -1.0, -1.5, -2.5, -124.5], device=cuda_device)])
+    y = torch.empty_like(x)
+    ext().attn_exp2_poly(x, y)
+    ref = torch.exp2(x)
+    rel = ((y - ref).abs() / ref).max().item()
+    assert rel < 1e-4, rel  # fitted bound 7.5e-5; bf16 P needs 2^-9
+    y2 = torch.empty(1, device=cuda_device)
+    ext().attn_exp2_poly(torch.tensor([float("-inf")], device=cuda_device), y2)
+    assert 0 <= y2.item() < 1e-37
