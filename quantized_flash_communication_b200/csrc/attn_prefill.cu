@@ -376,25 +376,27 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) 
         // S of this tile completed after the previous PV of this tile (in-order tensor pipe),
         // so O holds every earlier tile and may be rescaled here.
         float alpha = 1.f;
-        if (j == 0 || mx > m_ref + kRescaleLog2) {
+        const bool move = j == 0 || mx > m_ref + kRescaleLog2;
+        if (move) {
           const float m_new = fmaxf(m_ref, mx);
           const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-          if (j > 0) {
-            alpha = ex2(m_ref - m_use);
-            // O row *= alpha, in TMEM
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-              uint32_t u[32];
-              tc::tmem_ld_32x32b_x32(o_col + c * 32, u);
-              tc::tmem_wait_ld();
-              tc::tmem_reg_fence(u);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
-              tc::tmem_st_32x32b_x32(o_col + c * 32, u);
-            }
-            tc::tmem_wait_st();
-          }
+          if (j > 0) alpha = ex2(m_ref - m_use);
           m_ref = m_use;
+        }
+        // O rows *= alpha, in TMEM.  tcgen05.ld / st are warp-collective, so the whole warp
+        // rescales when any of its rows moved its maximum (the others multiply by 1).
+        if (j > 0 && __any_sync(QFC_FULL_MASK, move)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t u[32];
+            tc::tmem_ld_32x32b_x32(o_col + c * 32, u);
+            tc::tmem_wait_ld();
+            tc::tmem_reg_fence(u);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
+            tc::tmem_st_32x32b_x32(o_col + c * 32, u);
+          }
+          tc::tmem_wait_st();
         }
         float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll

@@ -47,3 +47,21 @@ def test_fma_pipe_exp2_against_exp2f(cuda_device):
     y2 = torch.empty(1, device=cuda_device)
     ext().attn_exp2_poly(torch.tensor([float("-inf")], device=cuda_device), y2)
     assert 0 <= y2.item() < 1e-37
+
+
+@pytest.mark.parametrize("B,S,nq,nkv", [(2, 1024, 4, 4), (1, 2048, 8, 2)])
+def test_prefill_attention_row_maxima_that_grow(cuda_device, B, S, nq, nkv):
+    """Keys whose scale grows along the sequence make the running maximum of some rows (not
+    all) jump by more than 2^8 between tiles: the lazy O rescale runs for part of a warp."""
+    hd = 128
+    g = torch.Generator(device="cpu").manual_seed(S + nq)
+    x = torch.randn(B * S, nq + 2 * nkv, hd, generator=g)
+    ramp = 1.0 + 6.0 * torch.arange(S).float().repeat(B) / S          # later keys score higher
+    x[:, nq:nq + nkv] *= ramp[:, None, None]
+    x[:, :nq] *= (0.5 + torch.rand(B * S, nq, 1, generator=g) * 2.5)   # rows differ in sharpness
+    qkv = x.reshape(B * S, -1).to(cuda_device, torch.bfloat16)
+    o = prefill_attention(qkv, B, S, nq, nkv, hd)
+    torch.cuda.synchronize()
+    assert attn_status(clear=True) == 0
+    ref = _ref(qkv, B, S, nq, nkv, hd)
+    assert rel_l2(o.float(), ref) < 1e-2
