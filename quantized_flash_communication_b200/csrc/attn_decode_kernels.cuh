@@ -9,6 +9,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "smem_optin.h"
 
 namespace qfc {
 namespace decode {
@@ -525,21 +526,6 @@ decode_partial_mma_kernel(const T* __restrict__ q, const T* __restrict__ kc, con
       part_ml[pi * 2 + 1] = Ls;
     }
   }
-}
-
-// Opts a kernel into more than 48 KB of dynamic shared memory on the CURRENT device.
-// The attribute belongs to one device's context, so the opt-in is tracked per device
-// (one bit per device in `done`); a process that launches on several GPUs sets it on each.
-template <typename Kern>
-inline cudaError_t opt_in_smem_per_device(Kern kern, int bytes, std::atomic<unsigned long long>& done) {
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
-  if (err != cudaSuccess) return err;
-  const unsigned long long bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
-  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
-  err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (err == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
-  return err;
 }
 
 template <typename T, int HD, int G>

@@ -39,6 +39,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "smem_optin.h"
 #include "tcgen05.cuh"
 
 namespace qfc {
@@ -513,12 +514,9 @@ void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_
   if (B == 0 || S == 0) return;
   c10::cuda::CUDAGuard guard(qkv.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  static bool attr_set[64] = {false};
+  static std::atomic<unsigned long long> smem_set{0};
   const int dev = qkv.get_device();
-  if (!attr_set[dev]) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr_set[dev] = true;
-  }
+  C10_CUDA_CHECK(opt_in_smem_per_device(attn_prefill_kernel, SMEM_BYTES, smem_set));
   const CUtensorMap tq = make_map(qkv.data_ptr(), B * S, (nq + 2 * nkv) * HD, (nq + 2 * nkv) * HD);
   Args a;
   a.B = (int)B;

@@ -40,6 +40,7 @@
 
 #include "common.cuh"
 #include "scatter.h"
+#include "smem_optin.h"
 #include "tcgen05.cuh"
 
 namespace qfc {
@@ -758,12 +759,9 @@ void launch_cfg(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& a,
   using C = Cfg<PAIR>;
   constexpr int smem = C::SMEM_BYTES + (is_qs(EPI) ? QS_STAGE_BYTES : 0);
   static_assert(smem <= 232448, "GEMM shared memory exceeds 227 KiB");
-  static bool attr_set[64] = {false};
+  static std::atomic<unsigned long long> smem_set{0};
   auto kern = gemm_bf16_kernel<EPI, PAIR>;
-  if (!attr_set[dev]) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set[dev] = true;
-  }
+  C10_CUDA_CHECK(opt_in_smem_per_device(kern, smem, smem_set));
   const int tiles = ((M + C::TILE_M - 1) / C::TILE_M) * a.n_tiles;
   const int per_unit = PAIR ? 2 : 1;
   GemmArgs args = a;
@@ -1138,11 +1136,8 @@ int* small_counters(int dev, int tiles) {
 void launch_small(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const at::Tensor* R, double timeout_ms) {
   const int M = (int)a.size(0), K = (int)a.size(1), N = (int)b.size(0);
   const int dev = a.get_device();
-  static bool attr_set[64] = {false};
-  if (!attr_set[dev]) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES_S));
-    attr_set[dev] = true;
-  }
+  static std::atomic<unsigned long long> smem_set{0};
+  C10_CUDA_CHECK(opt_in_smem_per_device(gemm_small_kernel, SMEM_BYTES_S, smem_set));
   SArgs s;
   std::memset(&s, 0, sizeof(s));
   s.M = M;
