@@ -45,7 +45,7 @@ def _parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch kernels eagerly instead of one CUDA graph")
     ap.add_argument("--seq-parallel", action="store_true",
-                    help="sequence-parallel residual stream: the all-reduces also add the residual and normalise")
+                    help="sequence-parallel residual stream at every world size (the default turns it on from 2 ranks)")
     ap.add_argument("--breakdown", action="store_true",
                     help="print per-operator device times of eager steps instead of the benchmark line")
     ap.add_argument("--no-fuse-gemm", action="store_true",

@@ -71,10 +71,11 @@ class TPContext:
         self.fuse_gemm = fuse_gemm and group_size == 128
         self.fuse_min_rows = 256  # below this, messages go one-shot through the plain kernel
         # The fused epilogue stores each row's 128-byte group to its owner with 16-byte
-        # stores 4 KiB apart; from 4 ranks on, most of the tile crosses NVLink that way and
-        # the GEMM followed by the standalone all-reduce kernel is faster (measured at 4
-        # ranks: 17.7 ms vs 25.6 ms per Llama-2-7B prefill step for o_proj + down_proj).
-        self.fuse_max_world = int(os.environ.get("QFC_FUSE_MAX_WORLD", "2"))
+        # stores 4 KiB apart, so at 8 ranks 7/8 of every tile crosses NVLink in that pattern
+        # and the GEMM followed by the standalone all-reduce kernel is faster.  Measured on
+        # the Llama-2-7B prefill step (8 x 1024 tokens, INT8, sequence-parallel residual):
+        # 4 ranks 30.25 ms fused vs 32.18 ms unfused, 8 ranks 24.56 ms vs 23.20 ms.
+        self.fuse_max_world = int(os.environ.get("QFC_FUSE_MAX_WORLD", "4"))
         self.timer = None  # utils.trace.OpTimer shared with the model when attached
         self.ar: Optional[QuantAllReduce] = None
         if self.world > 1 and ar_backend == "qfc":
@@ -85,10 +86,15 @@ class TPContext:
         # Sequence-parallel residual stream for prefill: each rank keeps rows
         # [r*R, (r+1)*R) of the residual and the row-parallel all-reduces also add the
         # residual and apply the next RMSNorm on those rows (csrc/allreduce_norm.cuh), so
-        # only the normalised activations are all-gathered.  Off unless requested
-        # (seq_parallel=True or QFC_SEQ_PARALLEL=1).
+        # only the normalised activations are all-gathered.  Default (seq_parallel=None):
+        # on from ``sp_min_world`` ranks (QFC_SEQ_PARALLEL=1 / 0 forces it on / off).  On the
+        # Llama-2-7B prefill step (8 x 1024 tokens, INT8) it takes the fused-epilogue step
+        # from 53.12 to 51.17 ms at 2 ranks and from 32.59 to 30.25 ms at 4, and the
+        # unfused step from 24.66 to 23.20 ms at 8.
+        self.sp_min_world = int(os.environ.get("QFC_SP_MIN_WORLD", "2"))
         if seq_parallel is None:
-            seq_parallel = os.environ.get("QFC_SEQ_PARALLEL", "0") == "1"
+            env = os.environ.get("QFC_SEQ_PARALLEL")
+            seq_parallel = (env == "1") if env is not None else self.world >= self.sp_min_world
         self.seq_parallel = bool(seq_parallel) and self.ar is not None and group_size == 128
         if self.seq_parallel and reserve_tokens and hidden_size:
             self.ar.reserve_rows(reserve_tokens, hidden_size, bits_options=(bits, 16))
