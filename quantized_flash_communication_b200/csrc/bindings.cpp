@@ -4,6 +4,7 @@
 
 #include <memory>
 
+#include "nvtx_range.h"
 #include "workspace.h"
 
 namespace qfc {
@@ -76,13 +77,15 @@ namespace py = pybind11;
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "B200-native kernels for quantized tensor-parallel communication";
+  m.def("set_nvtx", &qfc::set_nvtx, "turn the NVTX range around every CUDA op on or off", py::arg("on"));
+  m.def("nvtx_enabled", &qfc::nvtx_enabled);
 
-  m.def("quantize", &qfc::quantize_cuda, "blockwise quantize (CUDA)", py::arg("x"), py::arg("bits"),
+  m.def("quantize", qfc::traced("quantize", &qfc::quantize_cuda), "blockwise quantize (CUDA)", py::arg("x"), py::arg("bits"),
         py::arg("group_size"), py::arg("sym"), py::arg("scale_fp32"));
-  m.def("dequantize", &qfc::dequantize_cuda, "blockwise dequantize (CUDA)", py::arg("q"), py::arg("s"),
+  m.def("dequantize", qfc::traced("dequantize", &qfc::dequantize_cuda), "blockwise dequantize (CUDA)", py::arg("q"), py::arg("s"),
         py::arg("z"), py::arg("group_size"), py::arg("out_dtype"));
-  m.def("pack_int4", &qfc::pack_int4_cuda, "pack 4-bit codes into int32 words (CUDA)");
-  m.def("unpack_int4", &qfc::unpack_int4_cuda, "unpack int32 words into fp16 codes (CUDA)");
+  m.def("pack_int4", qfc::traced("pack_int4", &qfc::pack_int4_cuda), "pack 4-bit codes into int32 words (CUDA)");
+  m.def("unpack_int4", qfc::traced("unpack_int4", &qfc::unpack_int4_cuda), "unpack int32 words into fp16 codes (CUDA)");
 
   m.def("quantize_cpu", &qfc::quantize_cpu, "blockwise quantize (C++ CPU oracle)");
   m.def("dequantize_cpu", &qfc::dequantize_cpu, "blockwise dequantize (C++ CPU oracle)");
@@ -106,45 +109,45 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("os_bytes", &qfc::Workspace::os_bytes)
       .def_property_readonly("peers_ready", &qfc::Workspace::peers_ready);
 
-  m.def("gemm_qkv_rope", &qfc::gemm_qkv_rope, "qkv GEMM with RoPE and the KV-cache write in its epilogue",
+  m.def("gemm_qkv_rope", qfc::traced("gemm_qkv_rope", &qfc::gemm_qkv_rope), "qkv GEMM with RoPE and the KV-cache write in its epilogue",
         py::arg("a"), py::arg("w"), py::arg("out"), py::arg("pos"), py::arg("cos_sin"), py::arg("k_cache") = py::none(),
         py::arg("v_cache") = py::none(), py::arg("slots") = py::none(), py::arg("nq"), py::arg("nkv"),
         py::arg("timeout_ms") = 10000.0);
-  m.def("gemm_bf16", &qfc::gemm_bf16, "tcgen05 GEMM a @ b^T with fused epilogue (0 store, 1 swiglu, 2 residual)",
+  m.def("gemm_bf16", qfc::traced("gemm_bf16", &qfc::gemm_bf16), "tcgen05 GEMM a @ b^T with fused epilogue (0 store, 1 swiglu, 2 residual)",
         py::arg("a"), py::arg("b"), py::arg("out") = py::none(), py::arg("epi") = 0,
         py::arg("residual") = py::none(), py::arg("timeout_ms") = 10000.0, py::arg("max_ctas") = 0);
   m.def("gemm_status", &qfc::gemm_status, py::arg("clear") = false);
-  m.def("rmsnorm", &qfc::rmsnorm_cuda, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("y"), py::arg("eps"));
-  m.def("rope_kv_decode", &qfc::rope_kv_decode_cuda, "RoPE + paged KV write of one decode token per sequence");
-  m.def("rope_kv", &qfc::rope_kv_cuda, py::arg("qkv"), py::arg("pos"), py::arg("cos_sin"), py::arg("k_cache"),
+  m.def("rmsnorm", qfc::traced("rmsnorm", &qfc::rmsnorm_cuda), py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("y"), py::arg("eps"));
+  m.def("rope_kv_decode", qfc::traced("rope_kv_decode", &qfc::rope_kv_decode_cuda), "RoPE + paged KV write of one decode token per sequence");
+  m.def("rope_kv", qfc::traced("rope_kv", &qfc::rope_kv_cuda), py::arg("qkv"), py::arg("pos"), py::arg("cos_sin"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("slot_mapping"), py::arg("nq"), py::arg("nkv"), py::arg("hd"));
-  m.def("silu_mul", &qfc::silu_mul_cuda);
-  m.def("embedding", &qfc::embedding_cuda);
-  m.def("argmax", &qfc::argmax_cuda, py::arg("logits"), py::arg("best_val"), py::arg("best_idx"),
+  m.def("silu_mul", qfc::traced("silu_mul", &qfc::silu_mul_cuda));
+  m.def("embedding", qfc::traced("embedding", &qfc::embedding_cuda));
+  m.def("argmax", qfc::traced("argmax", &qfc::argmax_cuda), py::arg("logits"), py::arg("best_val"), py::arg("best_idx"),
         py::arg("idx_offset") = 0, py::arg("valid") = -1, py::arg("rng") = py::none(), py::arg("inv_temp") = 1.0,
         py::arg("done") = py::none());
-  m.def("attn_decode", &qfc::attn_decode_cuda, "paged split-KV decode attention");
-  m.def("attn_prefill", &qfc::attn_prefill_cuda, "causal flash prefill attention (tcgen05)");
-  m.def("attn_exp2_poly", &qfc::attn_exp2_poly, "2^x as the prefill softmax evaluates it on the FMA pipe");
+  m.def("attn_decode", qfc::traced("attn_decode", &qfc::attn_decode_cuda), "paged split-KV decode attention");
+  m.def("attn_prefill", qfc::traced("attn_prefill", &qfc::attn_prefill_cuda), "causal flash prefill attention (tcgen05)");
+  m.def("attn_exp2_poly", qfc::traced("attn_exp2_poly", &qfc::attn_exp2_poly), "2^x as the prefill softmax evaluates it on the FMA pipe");
   m.def("attn_status", &qfc::attn_status, py::arg("clear") = false);
 
   m.def("ar_plan", &qfc::ar_plan, "region sizes a quantized all-reduce call needs");
-  m.def("quant_all_reduce", &qfc::quant_all_reduce, "fused quantized all-reduce over peer memory",
+  m.def("quant_all_reduce", qfc::traced("quant_all_reduce", &qfc::quant_all_reduce), "fused quantized all-reduce over peer memory",
         py::arg("workspaces"), py::arg("ins"), py::arg("outs"), py::arg("bits"), py::arg("group_size"),
         py::arg("sym"), py::arg("scale_fp32"), py::arg("one_shot"), py::arg("quantize_local"),
         py::arg("timeout_ms"));
-  m.def("argmax_gather", &qfc::argmax_gather, "cross-rank argmax of (score, index) pairs (one kernel)");
-  m.def("gemm_all_reduce", &qfc::gemm_all_reduce,
+  m.def("argmax_gather", qfc::traced("argmax_gather", &qfc::argmax_gather), "cross-rank argmax of (score, index) pairs (one kernel)");
+  m.def("gemm_all_reduce", qfc::traced("gemm_all_reduce", &qfc::gemm_all_reduce),
         "all_reduce(a @ w^T) with the quantize-and-scatter fused into the GEMM epilogue", py::arg("workspace"),
         py::arg("a"), py::arg("w"), py::arg("out"), py::arg("bits"), py::arg("group_size"), py::arg("sym"),
         py::arg("scale_fp32"), py::arg("timeout_ms"));
   m.def("ar_plan_rows", &qfc::ar_plan_rows, "region sizes of a row-blocked (sequence-parallel) all-reduce + norm");
-  m.def("quant_all_reduce_norm", &qfc::quant_all_reduce_norm,
+  m.def("quant_all_reduce_norm", qfc::traced("quant_all_reduce_norm", &qfc::quant_all_reduce_norm),
         "x = all_gather(rmsnorm(h_shard += reduce_scatter(partial)) * w), one kernel over peer memory",
         py::arg("workspaces"), py::arg("partials"), py::arg("residual_shards"), py::arg("weight"), py::arg("outs"),
         py::arg("bits"), py::arg("sym"), py::arg("scale_fp32"), py::arg("quantize_local"), py::arg("eps"),
         py::arg("timeout_ms"));
-  m.def("gemm_all_reduce_norm", &qfc::gemm_all_reduce_norm,
+  m.def("gemm_all_reduce_norm", qfc::traced("gemm_all_reduce_norm", &qfc::gemm_all_reduce_norm),
         "the same with the reduce-scatter fused into the row-parallel GEMM's epilogue", py::arg("workspace"),
         py::arg("a"), py::arg("w"), py::arg("residual_shard"), py::arg("weight"), py::arg("out"), py::arg("bits"),
         py::arg("sym"), py::arg("scale_fp32"), py::arg("eps"), py::arg("timeout_ms"));

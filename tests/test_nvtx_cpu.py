@@ -1,0 +1,50 @@
+"""NVTX ranges: the switch reaches the native extension, wrapped ops keep their
+signatures (keywords, defaults, in-place outputs) and an op's error still propagates."""
+import pytest
+import torch
+
+from quantized_flash_communication_b200._ext import _load
+from quantized_flash_communication_b200.utils import trace
+
+C = _load()
+pytestmark = pytest.mark.skipif(C is None, reason="native extension not built")
+
+
+def test_switch_reaches_extension():
+    was = trace.nvtx_enabled()
+    try:
+        trace.set_nvtx(True)
+        assert C.nvtx_enabled() and trace.nvtx_enabled()
+        trace.set_nvtx(False)
+        assert not C.nvtx_enabled() and not trace.nvtx_enabled()
+    finally:
+        trace.set_nvtx(was)
+
+
+@pytest.mark.parametrize("on", [False, True])
+def test_wrapped_op_keeps_signature_and_errors(on):
+    was = trace.nvtx_enabled()
+    try:
+        trace.set_nvtx(on)
+        x = torch.randn(4, 128)
+        # keyword arguments and defaults are those of the unwrapped op
+        with pytest.raises(RuntimeError):  # CPU tensor: the CUDA op refuses it
+            C.argmax(logits=x, best_val=torch.empty(4), best_idx=torch.empty(4, dtype=torch.int64))
+        with pytest.raises(TypeError):  # unknown keyword: pybind11 rejects it before the call
+            C.gemm_bf16(x, x, nonexistent=1)
+    finally:
+        trace.set_nvtx(was)
+
+
+def test_python_regions_nest_with_timer_absent():
+    was = trace.nvtx_enabled()
+    try:
+        trace.set_nvtx(True)
+        with trace.maybe_region(None, "outer"):
+            with trace.maybe_region(None, "inner"):
+                y = torch.ones(3) * 2
+        assert torch.equal(y, torch.full((3,), 2.0))
+        trace.set_nvtx(False)
+        assert isinstance(trace.maybe_region(None, "x"), type(trace.contextlib.nullcontext()))
+    finally:
+        trace.set_nvtx(was)
