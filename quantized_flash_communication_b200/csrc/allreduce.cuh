@@ -444,17 +444,31 @@ __global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ A
   OutT* out = static_cast<OutT*>(p.out[rank]);
   char* my = p.base[rank];
   uint32_t* ep = p.epochs[rank] + ALG_ONE_SHOT * kMaxBlocks + b;
-  __shared__ uint32_t s_e;
+  uint32_t* calls = p.epochs[rank] + ALG_ONE_SHOT * kMaxBlocks + kOneShotCallsWord;
+  uint32_t* done = p.epochs[rank] + ALG_ONE_SHOT * kMaxBlocks + kOneShotDoneWord;
+  __shared__ uint32_t s_e, s_par;
   __shared__ int s_abort;
   if (threadIdx.x == 0) {
     s_e = *ep + 1u;
+    s_par = *calls & 1u;
     s_abort = 0;
   }
   __syncthreads();
   const uint32_t e = s_e;
-  // Double-buffered by epoch parity: a peer may start call k+1 while this rank still
-  // reads call k's slots.
-  const int64_t region = p.os_off + (int64_t)(e & 1u) * p.os_bytes;
+  // Double-buffered: a peer may start call k+1 while this rank still reads call k's
+  // slots.  The region is chosen by the parity of the rank's one-shot call count, the
+  // same for every block of a call.  (A block's own epoch would not do: when the grid
+  // changes between calls, a unit moves to a block whose epoch has another parity, and a
+  // fast rank's call k+1 could then overwrite call k's slots while they are read.)
+  const int64_t region = p.os_off + (int64_t)s_par * p.os_bytes;
+  // The last CTA of this rank to finish (also after a timed-out wait) advances the call
+  // count; every CTA has read it by then, and the next call is a later kernel.
+  auto finish = [&]() {
+    if (threadIdx.x == 0 && atomicAdd(done, 1u) == gridDim.x - 1) {
+      *done = 0u;
+      *calls = *calls + 1u;
+    }
+  };
   const int64_t units = p.chunk >> 8;
   const int64_t ustride = (int64_t)gridDim.x * wpb;
   const int64_t u0 = (int64_t)b * wpb + warp;
@@ -486,7 +500,10 @@ __global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ A
   __syncthreads();
   if ((int)threadIdx.x < W && (int)threadIdx.x != rank)
     st_release_sys(flag_at(p.base[threadIdx.x], PH_OS, b, rank), e);
-  if (!wait_sources(p, my, PH_OS, b, rank, W, e, true, &s_abort)) return;
+  if (!wait_sources(p, my, PH_OS, b, rank, W, e, true, &s_abort)) {
+    finish();
+    return;
+  }
 
   constexpr int NW = WC > 0 ? WC : kMaxRanks;
   constexpr int NU = (WC > 0 && kBatch / NW > 1) ? kBatch / NW : 1;
@@ -536,6 +553,7 @@ __global__ void __launch_bounds__(512) one_shot_kernel(const __grid_constant__ A
     }
   }
   if (threadIdx.x == 0) *ep = e;
+  finish();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1007,6 +1025,7 @@ void launch_ar(Kern kern, const ARParams& prm, int64_t units, int W_emul, int de
   // every CTA must be resident at once (CTA b waits for CTA b of the other ranks)
   int64_t cap = (int64_t)occ * sms / std::max(1, W_emul);
   cap = std::min<int64_t>(cap, max_wpb < 16 ? (int64_t)kMaxBlocks : std::min<int64_t>(sms, kMaxBlocks));
+  cap = std::min<int64_t>(cap, kOneShotDoneWord);  // the one-shot row keeps its last two words
   TORCH_CHECK(cap >= 1, "quant_all_reduce: no co-resident CTA budget (emulated world too large)");
   const int64_t G = std::max<int64_t>(1, std::min<int64_t>((units + wpb - 1) / wpb, cap));
   dim3 grid((unsigned)G, (unsigned)std::max(1, W_emul));

@@ -10,7 +10,8 @@
 //   [kFlagBytes, + kArgmaxBytes)        argmax gather slots, double-buffered by epoch parity
 //   [rs_off, rs_off + rs_bytes)         two-shot reduce-scatter slots (one per source rank)
 //   [ag_off, ag_off + ag_bytes)         two-shot all-gather slots      (one per source rank)
-//   [os_off, os_off + 2 * os_bytes)     one-shot slots, double-buffered by epoch parity
+//   [os_off, os_off + 2 * os_bytes)     one-shot slots, double-buffered by the parity of the
+//                                       rank's count of one-shot calls
 // Per-block epoch counters and the host-mapped status word are local to the rank.
 //
 // The reference has no counterpart: it moves every byte through NCCL collectives
@@ -35,6 +36,12 @@ constexpr int64_t kFlagBytes = (int64_t)kFlagPhases * kMaxBlocks * kMaxRanks * s
 // Cross-rank argmax: up to kArgmaxRows (score, index) pairs of 8 bytes per source rank.
 constexpr int64_t kArgmaxRows = 512;
 constexpr int64_t kArgmaxBytes = 2 * kMaxRanks * kArgmaxRows * 8;
+
+// Two words of the one-shot epoch row that are not block epochs (the one-shot grid stays
+// below them): the rank's count of finished one-shot calls, whose parity selects the slot
+// region of a call, and the number of CTAs of the running call that have finished.
+constexpr int kOneShotCallsWord = kMaxBlocks - 1;
+constexpr int kOneShotDoneWord = kMaxBlocks - 2;
 
 enum FlagPhase : int { PH_RS = 0, PH_AG = 1, PH_OS = 2, PH_GEMM = 3, PH_ARGMAX = 4 };
 enum EpochAlgo : int { ALG_TWO_SHOT = 0, ALG_ONE_SHOT = 1, ALG_GEMM_RS = 2, ALG_GEMM_AG = 3, ALG_ARGMAX = 4 };

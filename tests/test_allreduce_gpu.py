@@ -69,6 +69,28 @@ def test_emulated_matches_oracle(cuda_device, W, bits, gs, mode, shape, algo, dt
         xs = [x.roll(1) for x in xs]
 
 
+def test_sizes_change_between_calls(cuda_device):
+    """One workspace, back-to-back calls whose sizes (and so grids) change, one-shot and
+    two-shot interleaved: the one-shot slot region follows the rank's call count, the
+    same in every block, so every call must still match the oracle on every rank."""
+    W = 4
+    ar = EmulatedQuantAllReduce(W, cuda_device, bits=8, group_size=128, quant_type="asym", algo="auto",
+                                timeout_ms=5000)
+    shapes = [(1, 4096), (64, 4096), (5, 1000), (16, 8192), (64, 4096), (1, 4096), (300, 4096), (7, 4096)]
+    for it, shape in enumerate(shapes):
+        xs = _inputs(W, shape, torch.bfloat16, cuda_device, seed=it)
+        one = xs[0].numel() * 2 <= ar.one_shot_max_bytes
+        outs = ar(xs)
+        ar.check()
+        cpu = [x.cpu() for x in xs]
+        if one:
+            ref = spec.one_shot_all_reduce_ref(cpu, 8, 128, "asym", torch.float16, torch.bfloat16)
+        else:
+            ref = spec.two_step_all_reduce_ref(cpu, 8, 128, "asym", torch.float16, torch.bfloat16)
+        for r in range(W):
+            assert torch.equal(outs[r].cpu(), ref), (it, shape, r)
+
+
 @pytest.mark.parametrize("scale_dtype", [torch.float32])
 def test_fp32_scales_and_fp16_output(cuda_device, scale_dtype):
     W = 4

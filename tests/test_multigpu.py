@@ -54,6 +54,20 @@ def _case_allreduce(rank, world):
             ref = fn(xs, bits, gs, mode, torch.float16, torch.bfloat16)
             ok = ok and torch.equal(y.cpu(), ref)
         res[(bits, gs, mode, shape, algo)] = ok
+    # one workspace, sizes (and so grids) changing between back-to-back calls, one rank
+    # lagging: the one-shot slot region must follow the call count, not a block's epoch
+    ar = QuantAllReduce(None, dev, bits=8, group_size=128, quant_type="asym", algo="auto", timeout_ms=5000)
+    ok = True
+    for it, shape in enumerate([(1, 4096), (64, 4096), (5, 1000), (16, 8192), (300, 4096), (7, 4096)] * 2):
+        xs = _inputs(world, shape, torch.bfloat16, 1000 + it)
+        if rank == it % world:
+            torch.cuda._sleep(100_000)  # this rank starts late; the others run ahead
+        y = ar(xs[rank].to(dev))
+        ar.check()
+        one = xs[0].numel() * 2 <= 512 * 1024
+        fn = spec.one_shot_all_reduce_ref if one else spec.two_step_all_reduce_ref
+        ok = ok and torch.equal(y.cpu(), fn(xs, 8, 128, "asym", torch.float16, torch.bfloat16))
+    res["sizes_change_between_calls"] = ok
     # reference-compatible API: fp16 output, host-timed latency
     xs = _inputs(world, (8, 4096), torch.float16, 7)
     y, ms = flash_all_reduce(xs[rank].to(dev), group_size=128, bits=8, quant_type="asym")

@@ -1,0 +1,75 @@
+"""Race and deadlock checks of the peer-memory all-reduce protocols (tests/protocol_model.py).
+
+Each case replays W ranks' CTAs through a sequence of calls whose message and grid sizes
+change from call to call, under a skewed random scheduler (one rank runs slower, so ranks
+drift whole calls apart), and checks that every slot read sees the value its source wrote
+for that call and that the run finishes.  The unsafe variants are negative controls: the
+checker must find their races.
+"""
+import random
+
+import pytest
+
+from protocol_model import Call, Model, ProtocolViolation, random_calls
+
+SEEDS = range(60)
+
+
+def _violations(algo, seeds=SEEDS, capacity_choices=(None,), calls=6):
+    bad = 0
+    for seed in seeds:
+        rng = random.Random(seed)
+        W = rng.choice([2, 3, 4, 8])
+        try:
+            Model(W, random_calls(rng, algo, calls), seed=seed, capacity=rng.choice(capacity_choices)).run()
+        except ProtocolViolation:
+            bad += 1
+    return bad
+
+
+@pytest.mark.parametrize("algo", ["two_shot", "one_shot", "two_shot_staged"])
+def test_protocol_has_no_race_or_deadlock(algo):
+    assert _violations(algo) == 0
+
+
+@pytest.mark.parametrize("algo", ["two_shot", "one_shot"])
+def test_progress_with_partial_residency(algo):
+    """Only 1-2 CTAs of a rank resident at a time, the rest dispatched in block order."""
+    assert _violations(algo, capacity_choices=(1, 2)) == 0
+
+
+def test_mixed_algorithms_share_the_workspace():
+    for seed in SEEDS:
+        rng = random.Random(seed)
+        calls = [Call(rng.choice(["two_shot", "one_shot"]), rng.randint(1, 20), 0) for _ in range(8)]
+        for c in calls:
+            c.grid = rng.randint(1, min(6, c.units))
+        Model(rng.choice([2, 4]), calls, seed=seed).run()
+
+
+@pytest.mark.parametrize("algo", ["one_shot_block", "two_shot_staged_shared"])
+def test_checker_finds_the_unsafe_variants(algo):
+    assert _violations(algo) > len(SEEDS) // 4
+
+
+def test_block_parity_is_safe_while_the_grid_is_fixed():
+    """The race of per-block parity needs a grid change between calls."""
+    for seed in SEEDS:
+        rng = random.Random(seed)
+        Model(rng.choice([2, 3, 4]), [Call("one_shot_block", rng.randint(4, 24), 4) for _ in range(6)],
+              seed=seed).run()
+
+
+def test_deadlock_is_reported():
+    """A rank that skips a call leaves its peers waiting: the model must say so."""
+    m = Model(2, [Call("two_shot", 4, 2)], seed=0)
+    m.calls = [Call("two_shot", 4, 2)]
+    orig = m._program
+
+    def prog(r, k, call, b):
+        if r == 1:
+            return iter(())  # rank 1's CTAs exit at once without taking part
+        return orig(r, k, call, b)
+    m._program = prog
+    with pytest.raises(ProtocolViolation, match="deadlock"):
+        m.run()
