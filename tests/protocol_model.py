@@ -25,6 +25,11 @@ Protocols (``algo`` of a call):
   one_shot        every rank pushes its whole tensor; slots double-buffered by the parity
                   of the rank's one-shot call count, shared by all blocks of a call
                   (one_shot_kernel)
+  gemm_scatter + from_gemm   the GEMM-fed two-shot: the row-parallel GEMM's epilogue
+                  scatters into the reduce-scatter slots and publishes a per-rank GEMM
+                  epoch; the next kernel waits for every rank's epoch and runs phases 2-3
+                  (two calls of the list, always in this order)
+  argmax          the cross-rank argmax gather: one CTA, double-buffered by its epoch
   one_shot_block  the same with the parity taken from each block's own epoch.  Unsafe
                   when the grid changes between calls (a unit moves to a block whose epoch
                   has the other parity); the checker finds it, and the kernel uses the
@@ -184,8 +189,95 @@ class Model:
                 R.counters["one_shot_done"] = done
             yield None
 
+    def _gemm_scatter(self, r: int, k: int, call: Call, b: int) -> Iterator[Step]:
+        """A row-parallel GEMM whose epilogue stores every tile straight into its owner's
+        reduce-scatter slot, without waiting for anything; the last CTA to finish advances
+        the rank's GEMM epoch and publishes it to every rank (gemm.cu, EPI_QS*)."""
+        W, G, C = self.W, call.grid, call.units
+        R = self.ranks[r]
+        for j in range(W):                     # tile b covers units b, b + G, ... of every chunk
+            for u in range(b, C, G):
+                self._write(j, self._addr("rs", r, u, C), (k, r, u))
+                yield None
+        done = R.counters.get("gemm_done", 0) + 1
+        if done < G:
+            R.counters["gemm_done"] = done
+            return
+        R.counters["gemm_done"] = 0
+        eg = R.counters.get("gemm_epoch", 0) + 1
+        R.counters["gemm_epoch"] = eg
+        for j in range(W):
+            self._flag(j, ("gemm", 0, r), eg)
+            yield None
+
+    def _from_gemm(self, r: int, k: int, call: Call, b: int) -> Iterator[Step]:
+        """Phases 2 and 3 after _gemm_scatter (two_shot16_kernel<..., FROM_GEMM>): wait for
+        every rank's GEMM epoch, then reduce, all-gather and gather as the two-shot does.
+        The data it reads were written by the previous call of the list (the GEMM)."""
+        W, G, C = self.W, call.grid, call.units
+        R = self.ranks[r]
+        e = R.epochs.get(("two_shot", b), 0) + 1
+        eg = R.counters.get("gemm_epoch", 0)   # the value this rank's GEMM just published
+        kg = k - 1                             # the call index of the GEMM that wrote the slots
+        for src in range(W):
+            yield (lambda src=src: self._flag_geq(r, ("gemm", 0, src), eg))
+        mine = [u for u in range(C) if u % G == b]
+        for u in mine:
+            for src in range(W):
+                self._read(r, self._addr("rs", src, u, C), (kg, src, u), f"from_gemm phase 2 call {k}")
+                yield None
+            for j in range(W):
+                if j != r:
+                    self._write(j, self._addr("ag", r, u, C), (k, r, u))
+                    yield None
+        for j in range(W):
+            if j != r:
+                self._flag(j, ("ag", b, r), e)
+                yield None
+        for src in range(W):
+            if src != r:
+                yield (lambda src=src: self._flag_geq(r, ("ag", b, src), e))
+        for u in mine:
+            for src in range(W):
+                if src != r:
+                    self._read(r, self._addr("ag", src, u, C), (k, src, u), f"from_gemm phase 3 call {k}")
+                    yield None
+        R.epochs[("two_shot", b)] = e
+
+    def _argmax(self, r: int, k: int, call: Call, b: int) -> Iterator[Step]:
+        """argmax_gather_kernel: one CTA, (score, index) pairs pushed to every peer, slots
+        double-buffered by the parity of its single epoch, fixed slot stride."""
+        W, U = self.W, call.units
+        R = self.ranks[r]
+        e = R.epochs.get(("argmax", 0), 0) + 1
+        region = f"am{e & 1}"
+        for u in range(U):
+            for j in range(W):
+                if j != r:
+                    self._write(j, self._addr(region, r, u, 512), (k, r, u))
+                    yield None
+        for j in range(W):
+            if j != r:
+                self._flag(j, ("argmax", 0, r), e)
+                yield None
+        for src in range(W):
+            if src != r:
+                yield (lambda src=src: self._flag_geq(r, ("argmax", 0, src), e))
+        for u in range(U):
+            for src in range(W):
+                if src != r:
+                    self._read(r, self._addr(region, src, u, 512), (k, src, u), f"argmax call {k}")
+                    yield None
+        R.epochs[("argmax", 0)] = e
+
     def _program(self, r: int, k: int, call: Call, b: int) -> Iterator[Step]:
         a = call.algo
+        if a == "gemm_scatter":
+            return self._gemm_scatter(r, k, call, b)
+        if a == "from_gemm":
+            return self._from_gemm(r, k, call, b)
+        if a == "argmax":
+            return self._argmax(r, k, call, b)
         if a == "two_shot":
             return self._two_shot(r, k, call, b)
         if a == "two_shot_staged":
@@ -251,9 +343,18 @@ class Model:
 
 
 def random_calls(rng: random.Random, algo: str, n: int, max_units: int = 24, max_grid: int = 6) -> List[Call]:
-    """n calls of one algorithm with varying message and grid sizes."""
-    out = []
-    for _ in range(n):
+    """n calls of one algorithm (or of a random mix with algo == "mixed") with varying
+    message and grid sizes.  A GEMM-fed all-reduce is two calls: the GEMM, then phases 2-3."""
+    out: List[Call] = []
+    while len(out) < n:
+        a = rng.choice(["two_shot", "one_shot", "gemm", "argmax"]) if algo == "mixed" else algo
         units = rng.randint(1, max_units)
-        out.append(Call(algo, units, rng.randint(1, min(max_grid, units))))
+        grid = rng.randint(1, min(max_grid, units))
+        if a == "gemm":
+            out.append(Call("gemm_scatter", units, rng.randint(1, min(max_grid, units))))
+            out.append(Call("from_gemm", units, grid))
+        elif a == "argmax":
+            out.append(Call("argmax", min(units, 8), 1))
+        else:
+            out.append(Call(a, units, grid))
     return out

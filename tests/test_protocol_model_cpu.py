@@ -38,13 +38,15 @@ def test_progress_with_partial_residency(algo):
     assert _violations(algo, capacity_choices=(1, 2)) == 0
 
 
+@pytest.mark.parametrize("algo", ["gemm", "argmax"])
+def test_gemm_fed_and_argmax_protocols(algo):
+    assert _violations(algo, capacity_choices=(None, 2)) == 0
+
+
 def test_mixed_algorithms_share_the_workspace():
-    for seed in SEEDS:
-        rng = random.Random(seed)
-        calls = [Call(rng.choice(["two_shot", "one_shot"]), rng.randint(1, 20), 0) for _ in range(8)]
-        for c in calls:
-            c.grid = rng.randint(1, min(6, c.units))
-        Model(rng.choice([2, 4]), calls, seed=seed).run()
+    """Two-shot, one-shot, GEMM-fed two-shot and argmax calls back to back on one
+    workspace: the reduce-scatter slots are shared by the two-shot and the GEMM-fed path."""
+    assert _violations("mixed", calls=10, capacity_choices=(None, 2)) == 0
 
 
 @pytest.mark.parametrize("algo", ["one_shot_block", "two_shot_staged_shared"])
@@ -73,3 +75,27 @@ def test_deadlock_is_reported():
     m._program = prog
     with pytest.raises(ProtocolViolation, match="deadlock"):
         m.run()
+
+
+class _SkipWaits(Model):
+    """A mutant whose waits on one flag family always succeed."""
+    skip = ""
+
+    def _flag_geq(self, holder, key, e):
+        return True if key[0] == self.skip else super()._flag_geq(holder, key, e)
+
+
+@pytest.mark.parametrize("algo,skip", [("two_shot", "rs"), ("two_shot", "ag"), ("gemm", "gemm"),
+                                       ("one_shot", "os"), ("argmax", "argmax")])
+def test_checker_finds_a_missing_wait(algo, skip):
+    """Dropping any one wait of a protocol must show up as a stale or missing read."""
+    bad = 0
+    for seed in SEEDS:
+        rng = random.Random(seed)
+        m = type("Mutant", (_SkipWaits,), {"skip": skip})(rng.choice([2, 3, 4]), random_calls(rng, algo, 6),
+                                                             seed=seed)
+        try:
+            m.run()
+        except ProtocolViolation:
+            bad += 1
+    assert bad > len(SEEDS) // 4, bad
