@@ -26,6 +26,7 @@ import torch
 import torch.distributed as dist
 
 from ..communication import reset_communicators
+from ..parallel.quant_allreduce import set_norm_warps_per_row
 from ..parallel.quant_allreduce import QuantAllReduce
 from ..quantization import rel_l2
 from ..utils.dist import init_distributed
@@ -69,8 +70,9 @@ def _wire_bytes(n, W, bits, gs, one_shot):
     return (W - 1) / W * n * (per_elem(p1) + per_elem(p2))
 
 
-def _norm_point(ar, xs, tokens, hidden, bits, rank, W, dev, iters, t_ar):
-    """all-reduce + residual RMSNorm of every row vs the sequence-parallel kernel."""
+def _norm_point(ar, xs, tokens, hidden, bits, rank, W, dev, iters, t_ar, wprs=(1,)):
+    """all-reduce + residual RMSNorm of every row vs the sequence-parallel kernel (for each
+    of ``wprs`` warps per row)."""
     from ..ops import layers as L
     eps = 1e-5
     w = torch.ones(hidden, dtype=torch.bfloat16, device=dev)
@@ -91,12 +93,16 @@ def _norm_point(ar, xs, tokens, hidden, bits, rank, W, dev, iters, t_ar):
         ar.all_reduce_norm(xs, h_shard, w, eps, out=x_out)
 
     t_plain = _time(plain, iters)
-    t_sp = _time(fused, iters)
-    ar.check()
-    if rank == 0:
-        print(json.dumps({"impl": "allreduce_then_rmsnorm_vs_sequence_parallel", "W": W, "tokens": tokens,
-                          "hidden": hidden, "bits": bits, "allreduce_ms": t_ar, "allreduce_plus_rmsnorm_ms": t_plain,
-                          "allreduce_norm_sp_ms": t_sp, "speedup": t_plain / t_sp}), flush=True)
+    for wpr in wprs:
+        prev = set_norm_warps_per_row(wpr)
+        t_sp = _time(fused, iters)
+        set_norm_warps_per_row(prev)
+        ar.check()
+        if rank == 0:
+            print(json.dumps({"impl": "allreduce_then_rmsnorm_vs_sequence_parallel", "W": W, "tokens": tokens,
+                              "hidden": hidden, "bits": bits, "warps_per_row": wpr, "allreduce_ms": t_ar,
+                              "allreduce_plus_rmsnorm_ms": t_plain, "allreduce_norm_sp_ms": t_sp,
+                              "speedup": t_plain / t_sp}), flush=True)
 
 
 def main(argv=None):
@@ -109,6 +115,7 @@ def main(argv=None):
     ap.add_argument("--algo", default="auto")
     ap.add_argument("--reference", action="store_true")
     ap.add_argument("--norm", action="store_true")
+    ap.add_argument("--norm-wpr", default="1", help="warps per row of the sequence-parallel kernel, e.g. 1,2,4")
     args = ap.parse_args(argv)
     rank, W, dev = init_distributed()
     ar_cache = {}
@@ -162,7 +169,8 @@ def main(argv=None):
                     if rank0:
                         print(json.dumps(rec), flush=True)
                     if args.norm and gs == 128 and not one and hidden % 256 == 0:
-                        _norm_point(ar, xs, tokens, hidden, bits, rank, W, dev, args.iters, t)
+                        _norm_point(ar, xs, tokens, hidden, bits, rank, W, dev, args.iters, t,
+                                    wprs=_ints(args.norm_wpr))
     reset_communicators()
     ar_cache.clear()
     dist.destroy_process_group()

@@ -1,6 +1,8 @@
 // Host side of the sequence-parallel all-reduce + residual + RMSNorm (allreduce_norm.cuh):
 // argument checks, planning and dispatch, unfused (partial tensor in) and fused with the
 // row-parallel GEMM's quantize-and-scatter epilogue.
+#include <cstdlib>
+
 #include "allreduce_norm.cuh"
 #include "scatter.h"
 
@@ -17,6 +19,25 @@ using WsPtr = std::shared_ptr<Workspace>;
 std::vector<int64_t> ar_plan_rows(int64_t M, int64_t H, int64_t world, int64_t bits, bool scale_fp32) {
   const Plan pl = make_plan_rows(M, H, (int)world, (int)bits, scale_fp32);
   return {pl.chunk, pl.need_rs, pl.need_ag, pl.need_os};
+}
+
+namespace ar {
+int& norm_warps_per_row() {
+  static int wpr = [] {
+    const char* e = std::getenv("QFC_NORM_WARPS_PER_ROW");
+    const int v = e ? std::atoi(e) : 1;
+    return (v == 2 || v == 4 || v == 8) ? v : 1;
+  }();
+  return wpr;
+}
+}  // namespace ar
+
+// Warps per row of the sequence-parallel norm kernel (1, 2, 4 or 8); returns the previous value.
+int64_t set_norm_warps_per_row(int64_t wpr) {
+  TORCH_CHECK(wpr == 1 || wpr == 2 || wpr == 4 || wpr == 8, "set_norm_warps_per_row: 1, 2, 4 or 8");
+  const int prev = norm_warps_per_row();
+  norm_warps_per_row() = (int)wpr;
+  return prev;
 }
 
 namespace {

@@ -38,6 +38,7 @@ void quant_all_reduce_norm(const std::vector<std::shared_ptr<Workspace>>& wss, c
                            const std::vector<at::Tensor>& hs, const at::Tensor& weight,
                            const std::vector<at::Tensor>& xs, int64_t bits, bool sym, bool scale_fp32,
                            bool quantize_local, double eps, double timeout_ms);
+int64_t set_norm_warps_per_row(int64_t wpr);
 void gemm_all_reduce_norm(const std::shared_ptr<Workspace>& ws, const at::Tensor& a, const at::Tensor& w,
                           const at::Tensor& h, const at::Tensor& weight, at::Tensor& x, int64_t bits, bool sym,
                           bool scale_fp32, double eps, double timeout_ms);
@@ -141,6 +142,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "all_reduce(a @ w^T) with the quantize-and-scatter fused into the GEMM epilogue", py::arg("workspace"),
         py::arg("a"), py::arg("w"), py::arg("out"), py::arg("bits"), py::arg("group_size"), py::arg("sym"),
         py::arg("scale_fp32"), py::arg("timeout_ms"));
+  m.def("set_norm_warps_per_row", &qfc::set_norm_warps_per_row,
+        "warps per row of the sequence-parallel all-reduce + norm kernel (1, 2, 4 or 8); returns the previous value",
+        py::arg("wpr"));
   m.def("ar_plan_rows", &qfc::ar_plan_rows, "region sizes of a row-blocked (sequence-parallel) all-reduce + norm");
   m.def("quant_all_reduce_norm", qfc::traced("quant_all_reduce_norm", &qfc::quant_all_reduce_norm),
         "x = all_gather(rmsnorm(h_shard += reduce_scatter(partial)) * w), one kernel over peer memory",

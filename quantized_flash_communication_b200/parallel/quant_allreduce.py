@@ -17,7 +17,7 @@ import torch.distributed as dist
 from .._ext import ext
 from .symm_mem import EmulatedWorkspaces, SymmetricWorkspace, default_timeout_ms
 
-__all__ = ["QuantAllReduce", "EmulatedQuantAllReduce", "ONE_SHOT_MAX_BYTES"]
+__all__ = ["QuantAllReduce", "EmulatedQuantAllReduce", "ONE_SHOT_MAX_BYTES", "set_norm_warps_per_row"]
 
 # Messages up to this many input bytes use the one-shot algorithm under algo="auto".
 ONE_SHOT_MAX_BYTES = 512 * 1024
@@ -26,6 +26,14 @@ _OUT_PAIRS = {
     (torch.bfloat16, torch.bfloat16), (torch.bfloat16, torch.float16), (torch.float16, torch.float16),
     (torch.float32, torch.float32), (torch.float32, torch.float16),
 }
+
+
+def set_norm_warps_per_row(wpr: int) -> int:
+    """Warps that share a row in the sequence-parallel all-reduce + norm kernel (1, 2, 4
+    or 8; process-wide, initially QFC_NORM_WARPS_PER_ROW or 1).  Returns the previous
+    value.  More than one warp per row multiplies the kernel's grid, for row counts per
+    rank that leave SMs idle with one warp per row."""
+    return int(ext().set_norm_warps_per_row(int(wpr)))
 
 
 def _pick_one_shot(algo: str, nbytes: int, one_shot_max: int) -> bool:

@@ -1,5 +1,6 @@
-"""NVTX ranges: the switch reaches the native extension, wrapped ops keep their
-signatures (keywords, defaults, in-place outputs) and an op's error still propagates."""
+"""Host-side switches of the native extension.  NVTX ranges: the switch reaches the
+extension, wrapped ops keep their signatures (keywords, defaults, in-place outputs) and
+an op's error still propagates.  The warps-per-row switch of the sequence-parallel kernel."""
 import pytest
 import torch
 
@@ -48,3 +49,16 @@ def test_python_regions_nest_with_timer_absent():
         assert isinstance(trace.maybe_region(None, "x"), type(trace.contextlib.nullcontext()))
     finally:
         trace.set_nvtx(was)
+
+
+def test_norm_warps_per_row_switch():
+    """The sequence-parallel kernel's warps-per-row switch: values 1, 2, 4, 8, others refused."""
+    from quantized_flash_communication_b200.parallel.quant_allreduce import set_norm_warps_per_row
+    prev = set_norm_warps_per_row(4)
+    try:
+        assert set_norm_warps_per_row(2) == 4
+        with pytest.raises(RuntimeError):
+            set_norm_warps_per_row(3)
+        assert set_norm_warps_per_row(2) == 2
+    finally:
+        set_norm_warps_per_row(prev)
