@@ -34,6 +34,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAException.h>
 
+#include <atomic>
 #include <memory>
 
 #include "common.cuh"
@@ -1002,11 +1003,14 @@ inline Plan make_plan(int64_t n, int W, int bits, int gs, bool fp32, int in_elem
 }
 
 inline int num_sms(int dev) {
-  static int cached[64] = {0};
-  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  static std::atomic<int> cached[64] = {};  // threads may race to fill an entry: same value
+  if (dev >= 0 && dev < 64) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c) return c;
+  }
   int v = 0;
   cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-  if (dev >= 0 && dev < 64) cached[dev] = v;
+  if (dev >= 0 && dev < 64) cached[dev].store(v, std::memory_order_relaxed);
   return v;
 }
 

@@ -33,6 +33,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include <cstdlib>
@@ -724,6 +725,9 @@ bool split_k_enabled() {
 }
 
 // Per-device arrival counters of split-K tiles, zeroed once; each launch leaves them zero.
+// One set per device: split-K GEMMs that run at the same time on two streams of one
+// device would share them, so such GEMMs must be ordered (the models launch everything
+// on one stream).
 int* split_counters(int dev, int tiles) {
   constexpr int kMaxTiles = 1 << 14;
   static int* buf[64] = {nullptr};
@@ -749,9 +753,13 @@ bool pair_enabled() {
 }
 
 int sm_count(int dev) {
-  static int cached[64] = {0};
-  if (cached[dev] == 0) cudaDeviceGetAttribute(&cached[dev], cudaDevAttrMultiProcessorCount, dev);
-  return cached[dev];
+  static std::atomic<int> cached[64] = {};  // threads may race to fill an entry: same value
+  int v = cached[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
 }
 
 template <int EPI, bool PAIR>
