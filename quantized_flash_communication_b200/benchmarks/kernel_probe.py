@@ -37,7 +37,12 @@ def main(argv=None):
                                        "gemm_small", "qkv_rope"])
     ap.add_argument("shape", nargs="*", type=int)
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--attn-packed", action="store_true",
+                    help="attention: the softmax with packed two-lane fp32 arithmetic")
     args = ap.parse_args(argv)
+    if args.attn_packed:
+        from .._ext import ext
+        ext().set_attn_packed(True)
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
     if args.kernel == "gemm":

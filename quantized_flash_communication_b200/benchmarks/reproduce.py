@@ -88,7 +88,8 @@ def items(gpus: int) -> Dict[str, List[Tuple[int, List[str]]]]:
                                   "--new", "128", "--bits", "4"]))
     out["quant"] = [(1, ["-m", f"{PKG}.bench_quant", "--reference"])]
     probes = [["gemm"], ["attention", "8", "1024", "32", "32"], ["attention", "4", "2048", "64", "8"],
-              ["attention", "2", "4096", "32", "8"], ["allreduce", "2", "16384", "4096", "8"],
+              ["attention", "2", "4096", "32", "8"], ["attention", "8", "1024", "32", "32", "--attn-packed"],
+              ["attention", "4", "2048", "64", "8", "--attn-packed"], ["allreduce", "2", "16384", "4096", "8"],
               ["allreduce_norm", "8", "8192", "4096", "8"], ["quantize"], ["decode"], ["rmsnorm"], ["rope_decode"],
               ["silu_mul"], ["pack"], ["unpack"], ["oneshot"], ["gemm_qs8"], ["gemm_small"], ["qkv_rope"]]
     out["kernels"] = [(1, ["-m", f"{PKG}.kernel_probe"] + p + ["--iters", "10"]) for p in probes]

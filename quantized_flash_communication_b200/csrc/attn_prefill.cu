@@ -35,7 +35,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cfloat>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -97,9 +99,35 @@ QFC_DEV float ex2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(r) << 23));
 }
 
-__global__ void exp2_poly_kernel(const float* x, float* y, int64_t n) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    y[i] = ex2_poly(x[i]);
+// ex2_poly on a pair, with the packed fp32 FMA / add of sm_100 (two lanes per instruction).
+// Every lane performs the same roundings as ex2_poly: x - (r - M) is one fma(r', -1, x) of
+// the exact r' = r - M, and the cubic is the same chain of fused multiply-adds.
+QFC_DEV float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 r = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
+  const float2 t = __fadd2_rn(r, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(t, make_float2(-1.f, -1.f), x);
+  float2 p = __ffma2_rn(make_float2(kEx2C3, kEx2C3), f, make_float2(kEx2C2, kEx2C2));
+  p = __ffma2_rn(p, f, make_float2(kEx2C1, kEx2C1));
+  p = __ffma2_rn(p, f, make_float2(kEx2C0, kEx2C0));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(r.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(r.y) << 23)));
+}
+
+__global__ void exp2_poly_kernel(const float* x, float* y, int64_t n, bool pairs) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (!pairs) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) y[i] = ex2_poly(x[i]);
+    return;
+  }
+  // elements 2k and 2k + 1 as the two lanes of ex2_poly2
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; 2 * k < n; k += stride) {
+    const bool two = 2 * k + 1 < n;
+    const float2 r = ex2_poly2(make_float2(x[2 * k], two ? x[2 * k + 1] : 0.f));
+    y[2 * k] = r.x;
+    if (two) y[2 * k + 1] = r.y;
+  }
 }
 
 // Work item i -> (query tile pair, head, sequence); heaviest (last) pairs first.
@@ -118,6 +146,10 @@ QFC_DEV void item_tiles(int pr, const Args& a, int kv_tiles, int& na, int& nb) {
   nb = (qb < a.q_tiles) ? min(qb + 1, kv_tiles) : 0;
 }
 
+// PACKED: the softmax's scale-and-subtract, row sums and FMA-pipe exponentials use the
+// packed two-lane fp32 instructions (half the issue slots for that arithmetic); P is
+// bit-identical, the row sum l is added in another order.
+template <bool PACKED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) {
   extern __shared__ uint8_t smem_raw[];
@@ -400,25 +432,38 @@ attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQKV, const Args args) 
           tc::tmem_wait_st();
         }
         float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+        float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        const float2 sc2 = make_float2(args.scale_log2, args.scale_log2);
+        const float2 nm2 = make_float2(-m_ref, -m_ref);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {  // 4 chunks of 32 keys -> 16 TMEM columns of bf16 pairs
           uint32_t w[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
             // one pair in kPolyEvery on the FMA pipe, the rest on MUFU
-            const float a0 = fmaf(sv[c * 32 + 2 * q], args.scale_log2, -m_ref);
-            const float a1 = fmaf(sv[c * 32 + 2 * q + 1], args.scale_log2, -m_ref);
             const bool poly = kPolyEvery > 0 && (q % kPolyEvery) == kPolyEvery - 1;
-            const float p0 = poly ? ex2_poly(a0) : ex2(a0);
-            const float p1 = poly ? ex2_poly(a1) : ex2(a1);
-            sum4[q & 3] += p0 + p1;
+            float p0, p1;
+            if constexpr (PACKED) {
+              const float2 a = __ffma2_rn(make_float2(sv[c * 32 + 2 * q], sv[c * 32 + 2 * q + 1]), sc2, nm2);
+              const float2 pp = poly ? ex2_poly2(a) : make_float2(ex2(a.x), ex2(a.y));
+              sum2[q & 1] = __fadd2_rn(sum2[q & 1], pp);
+              p0 = pp.x;
+              p1 = pp.y;
+            } else {
+              const float a0 = fmaf(sv[c * 32 + 2 * q], args.scale_log2, -m_ref);
+              const float a1 = fmaf(sv[c * 32 + 2 * q + 1], args.scale_log2, -m_ref);
+              p0 = poly ? ex2_poly(a0) : ex2(a0);
+              p1 = poly ? ex2_poly(a1) : ex2(a1);
+              sum4[q & 3] += p0 + p1;
+            }
             w[q] = pack_bf16x2(p0, p1);  // key 2q in the low half
           }
           tc::tmem_st_32x32b_x16(s_col + c * 16, w);
         }
         tc::tmem_wait_st();
         tc::tc_fence_before();
-        l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+        if constexpr (PACKED) l = l * alpha + ((sum2[0].x + sum2[1].x) + (sum2[0].y + sum2[1].y));
+        else l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
         tc::mbar_arrive(tc::smem_u32(&p_full[t]));
       }
       if (!ok) break;
@@ -500,7 +545,19 @@ int* status_word() {
   return p;
 }
 
+// The packed-arithmetic softmax (attn_prefill_kernel<true>) is off unless QFC_ATTN_PACKED=1
+// or set_attn_packed(true): it has to win a measurement before it becomes the default.
+std::atomic<bool>& packed_flag() {
+  static std::atomic<bool> on{[] {
+    const char* e = std::getenv("QFC_ATTN_PACKED");
+    return e != nullptr && e[0] == '1';
+  }()};
+  return on;
+}
+
 }  // namespace attn
+
+bool set_attn_packed(bool on) { return attn::packed_flag().exchange(on); }
 
 // qkv [B*S, (nq + 2 nkv) * 128] bf16 (RoPE applied) -> out [B*S, nq * 128] bf16, causal.
 void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_t S, int64_t nq, int64_t nkv,
@@ -514,9 +571,11 @@ void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_
   if (B == 0 || S == 0) return;
   c10::cuda::CUDAGuard guard(qkv.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  static std::atomic<unsigned long long> smem_set{0};
+  static std::atomic<unsigned long long> smem_set{0}, smem_set_packed{0};
   const int dev = qkv.get_device();
-  C10_CUDA_CHECK(opt_in_smem_per_device(attn_prefill_kernel, SMEM_BYTES, smem_set));
+  const bool packed = packed_flag().load(std::memory_order_relaxed);
+  if (packed) C10_CUDA_CHECK(opt_in_smem_per_device(attn_prefill_kernel<true>, SMEM_BYTES, smem_set_packed));
+  else C10_CUDA_CHECK(opt_in_smem_per_device(attn_prefill_kernel<false>, SMEM_BYTES, smem_set));
   const CUtensorMap tq = make_map(qkv.data_ptr(), B * S, (nq + 2 * nkv) * HD, (nq + 2 * nkv) * HD);
   Args a;
   a.B = (int)B;
@@ -534,12 +593,14 @@ void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t items = (int64_t)a.q_pairs * nq * B;
   const int grid = (int)std::min<int64_t>(items, sms);
-  attn_prefill_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tq, a);
+  if (packed) attn_prefill_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tq, a);
+  else attn_prefill_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tq, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// y = 2^x through the softmax's FMA-pipe exponential (for tests against exp2f).
-void attn_exp2_poly(const at::Tensor& x, at::Tensor& y) {
+// y = 2^x through the softmax's FMA-pipe exponential (for tests against exp2f); pairs: the
+// packed two-lane form used by the packed softmax.
+void attn_exp2_poly(const at::Tensor& x, at::Tensor& y, bool pairs) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous() && y.sizes() == x.sizes() &&
                   y.scalar_type() == at::kFloat && y.is_contiguous(), "attn_exp2_poly: fp32 CUDA tensors");
   c10::cuda::CUDAGuard guard(x.device());
@@ -547,7 +608,7 @@ void attn_exp2_poly(const at::Tensor& x, at::Tensor& y) {
   if (n == 0) return;
   const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
   attn::exp2_poly_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(x.data_ptr<float>(),
-                                                                               y.data_ptr<float>(), n);
+                                                                               y.data_ptr<float>(), n, pairs);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

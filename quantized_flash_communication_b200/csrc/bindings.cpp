@@ -71,7 +71,8 @@ void attn_decode_cuda(const at::Tensor& q, const at::Tensor& kc, const at::Tenso
 void attn_prefill_cuda(const at::Tensor& qkv, at::Tensor& out, int64_t B, int64_t S, int64_t nq, int64_t nkv,
                        int64_t hd, double scale);
 int64_t attn_status(bool clear);
-void attn_exp2_poly(const at::Tensor& x, at::Tensor& y);
+bool set_attn_packed(bool on);
+void attn_exp2_poly(const at::Tensor& x, at::Tensor& y, bool pairs);
 }  // namespace qfc
 
 namespace py = pybind11;
@@ -129,8 +130,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("done") = py::none());
   m.def("attn_decode", qfc::traced("attn_decode", &qfc::attn_decode_cuda), "paged split-KV decode attention");
   m.def("attn_prefill", qfc::traced("attn_prefill", &qfc::attn_prefill_cuda), "causal flash prefill attention (tcgen05)");
-  m.def("attn_exp2_poly", qfc::traced("attn_exp2_poly", &qfc::attn_exp2_poly), "2^x as the prefill softmax evaluates it on the FMA pipe");
+  m.def("attn_exp2_poly", qfc::traced("attn_exp2_poly", &qfc::attn_exp2_poly),
+        "2^x as the prefill softmax evaluates it on the FMA pipe", py::arg("x"), py::arg("y"),
+        py::arg("pairs") = false);
   m.def("attn_status", &qfc::attn_status, py::arg("clear") = false);
+  m.def("set_attn_packed", &qfc::set_attn_packed,
+        "prefill attention softmax with packed two-lane fp32 arithmetic (off by default); returns the previous value",
+        py::arg("on"));
 
   m.def("ar_plan", &qfc::ar_plan, "region sizes a quantized all-reduce call needs");
   m.def("quant_all_reduce", qfc::traced("quant_all_reduce", &qfc::quant_all_reduce), "fused quantized all-reduce over peer memory",
