@@ -70,9 +70,10 @@ class TPContext:
         # quantize-and-scatter inside the row-parallel GEMMs' epilogue (two-shot, group 128)
         self.fuse_gemm = fuse_gemm and group_size == 128
         self.fuse_min_rows = 256  # below this, messages go one-shot through the plain kernel
-        # The fused epilogue stores each row's 128-byte group to its owner with 16-byte
-        # stores 4 KiB apart, so at 8 ranks 7/8 of every tile crosses NVLink in that pattern
-        # and the GEMM followed by the standalone all-reduce kernel is faster.  Measured on
+        # The fused epilogue stores every tile's quantized rows into their owners' slots, so
+        # at 8 ranks 7/8 of every tile leaves over NVLink from the GEMM's epilogue, whose
+        # store stream then paces the GEMM, and the GEMM followed by the standalone
+        # all-reduce kernel is faster.  Measured on
         # the Llama-2-7B prefill step (8 x 1024 tokens, INT8, sequence-parallel residual):
         # 4 ranks 30.25 ms fused vs 32.18 ms unfused, 8 ranks 24.56 ms vs 23.20 ms.
         self.fuse_max_world = int(os.environ.get("QFC_FUSE_MAX_WORLD", "4"))
