@@ -168,10 +168,19 @@ def test_gemm_fused_scatter_single_rank(cuda_device, bits, mode):
         assert torch.equal(fused.cpu(), ref)
 
 
+@pytest.fixture(params=[1, 2, 4], ids=["wpr1", "wpr2", "wpr4"])
+def norm_wpr(request):
+    """Warps per row of the sequence-parallel kernel (1: one warp per row, the default)."""
+    from quantized_flash_communication_b200.parallel.quant_allreduce import set_norm_warps_per_row
+    prev = set_norm_warps_per_row(request.param)
+    yield request.param
+    set_norm_warps_per_row(prev)
+
+
 @pytest.mark.parametrize("W,M,H,bits,mode", [(2, 256, 1024, 8, "asym"), (4, 1000, 4096, 8, "asym"),
                                                (8, 300, 2048, 4, "sym"), (3, 77, 512, 6, "asym"),
                                                (2, 64, 256, 16, "asym"), (1, 130, 1024, 8, "asym")])
-def test_emulated_all_reduce_norm(cuda_device, W, M, H, bits, mode):
+def test_emulated_all_reduce_norm(cuda_device, norm_wpr, W, M, H, bits, mode):
     """Sequence-parallel all-reduce + residual + RMSNorm: residual shards bit-exact with the
     oracle, x identical on every rank and equal to the oracle up to rsqrt rounding."""
     from quantized_flash_communication_b200.parallel import EmulatedQuantAllReduce
@@ -196,7 +205,7 @@ def test_emulated_all_reduce_norm(cuda_device, W, M, H, bits, mode):
         hs_in = h_ref  # the second call continues from the updated shards
 
 
-def test_gemm_fused_all_reduce_norm_single_rank(cuda_device):
+def test_gemm_fused_all_reduce_norm_single_rank(cuda_device, norm_wpr):
     """GEMM with the scatter epilogue + norm kernel == GEMM, then the norm all-reduce."""
     from quantized_flash_communication_b200.ops import gemm as G
     from quantized_flash_communication_b200.parallel import QuantAllReduce
