@@ -26,7 +26,7 @@ import torch
 import torch.distributed as dist
 
 from ..communication import reset_communicators
-from ..parallel.quant_allreduce import set_norm_warps_per_row
+from ..parallel.quant_allreduce import set_norm_warps_per_row, set_two_shot_stages
 from ..parallel.quant_allreduce import QuantAllReduce
 from ..quantization import rel_l2
 from ..utils.dist import init_distributed
@@ -116,6 +116,7 @@ def main(argv=None):
     ap.add_argument("--reference", action="store_true")
     ap.add_argument("--norm", action="store_true")
     ap.add_argument("--norm-wpr", default="1", help="warps per row of the sequence-parallel kernel, e.g. 1,2,4")
+    ap.add_argument("--stages", default="1", help="stages per CTA of the two-shot kernel, e.g. 1,2")
     args = ap.parse_args(argv)
     rank, W, dev = init_distributed()
     ar_cache = {}
@@ -158,6 +159,15 @@ def main(argv=None):
                            "busbw_gbs_equiv": 2.0 * (W - 1) / W * n * 2 / (t * 1e-3) / 1e9,
                            "speedup_vs_nccl": t_nccl / t, "rel_l2": err, "nvlink_bytes_per_rank": wb,
                            "roofline_ms": roof_ms, "roofline_frac": roof_ms / t}
+                    for st in _ints(args.stages):
+                        if st != 1 and not one:  # the staged kernel (two-shot only), same inputs
+                            prev = set_two_shot_stages(st)
+                            t_st = _time(lambda: ar(xs, out=out), args.iters)
+                            set_two_shot_stages(prev)
+                            ar.check()
+                            rec[f"ms_stages{st}"] = t_st
+                            rec[f"roofline_frac_stages{st}"] = roof_ms / t_st
+                            rec[f"stages{st}_bit_exact"] = bool(torch.equal(out, ar(xs)))
                     if ref_far is not None:
                         xr = xs.to(torch.float16)
                         t_ref = _time(lambda: ref_far(xr.clone(), group_size=gs, bits=bits, quant_type="asym"),

@@ -72,7 +72,8 @@ def items(gpus: int) -> Dict[str, List[Tuple[int, List[str]]]]:
     sweep = ["--tokens", "1,16,128,1024,4096,16384", "--hidden", "4096,8192", "--iters", "10"]
     out["allreduce"] = []
     for n in multi:
-        out["allreduce"].append((n, ["-m", f"{PKG}.bench_allreduce"] + sweep + ["--bits", "8,4", "--gs", "32,64,128"]))
+        out["allreduce"].append((n, ["-m", f"{PKG}.bench_allreduce"] + sweep + ["--bits", "8,4", "--gs", "32,64,128",
+                                                                              "--stages", "1,2"]))
         out["allreduce"].append((n, ["-m", f"{PKG}.bench_allreduce"] + sweep + ["--bits", "8,4", "--gs", "128",
                                                                               "--reference"]))
     out["norm"] = [(n, ["-m", f"{PKG}.bench_allreduce", "--tokens", "1024,8192", "--hidden", "4096", "--bits", "8",

@@ -2,6 +2,7 @@
 // The kernels are in allreduce.cuh and are instantiated per input dtype in
 // allreduce_inst_*.cu (compiled in parallel).
 #include <cfloat>
+#include <cstdlib>
 
 #include "allreduce.cuh"
 #include "scatter.h"
@@ -26,6 +27,24 @@ void gemm_qscatter(const at::Tensor& a, const at::Tensor& b, const ScatterArgs& 
 using namespace ar;
 
 using WsPtr = std::shared_ptr<Workspace>;
+
+namespace ar {
+int& two_shot_stages() {
+  static int stages = [] {
+    const char* e = std::getenv("QFC_AR_STAGES");
+    return (e && e[0] == '2') ? 2 : 1;
+  }();
+  return stages;
+}
+}  // namespace ar
+
+// Stages of the 16-per-lane two-shot all-reduce (1 or 2); returns the previous value.
+int64_t set_two_shot_stages(int64_t stages) {
+  TORCH_CHECK(stages == 1 || stages == 2, "set_two_shot_stages: 1 or 2");
+  const int prev = two_shot_stages();
+  two_shot_stages() = (int)stages;
+  return prev;
+}
 
 // Region sizes a call needs: (chunk, need_rs, need_ag, need_os) for the given algorithm.
 std::vector<int64_t> ar_plan(int64_t n, int64_t world, int64_t bits, int64_t gs, bool scale_fp32,

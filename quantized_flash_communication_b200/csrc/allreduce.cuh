@@ -946,6 +946,14 @@ __global__ void __launch_bounds__(kWarps16 * 32, 3) two_shot16_kernel(const __gr
   if (threadIdx.x == 0) *ep = e;
 }
 
+}  // namespace ar
+}  // namespace qfc
+
+#include "allreduce_staged.cuh"
+
+namespace qfc {
+namespace ar {
+
 // ---------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------
@@ -1028,14 +1036,19 @@ void launch_ar(Kern kern, const ARParams& prm, int64_t units, int W_emul, int de
   if (occ < 1) occ = 1;
   // every CTA must be resident at once (CTA b waits for CTA b of the other ranks)
   int64_t cap = (int64_t)occ * sms / std::max(1, W_emul);
-  cap = std::min<int64_t>(cap, max_wpb < 16 ? (int64_t)kMaxBlocks : std::min<int64_t>(sms, kMaxBlocks));
-  cap = std::min<int64_t>(cap, kOneShotDoneWord);  // the one-shot row keeps its last two words
+  // two-shot grids stay below kStageBlockOff (the staged kernel's second flag set); the
+  // one-shot row keeps its last two words
+  cap = std::min<int64_t>(cap, max_wpb < 16 ? (int64_t)kStageBlockOff : std::min<int64_t>(sms, kStageBlockOff));
   TORCH_CHECK(cap >= 1, "quant_all_reduce: no co-resident CTA budget (emulated world too large)");
   const int64_t G = std::max<int64_t>(1, std::min<int64_t>((units + wpb - 1) / wpb, cap));
   dim3 grid((unsigned)G, (unsigned)std::max(1, W_emul));
   kern<<<grid, threads, 0, st>>>(prm);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
+
+// Stages of the 16-per-lane two-shot kernel: 1 (two_shot16_kernel) or 2
+// (two_shot16s_kernel).  Process-wide; QFC_AR_STAGES sets the initial value.
+int& two_shot_stages();
 
 template <typename InT, typename OutT, int WC>
 void dispatch_bits_w(const ARParams& prm, const Plan& pl, bool one_shot, int64_t units, int W_emul, int dev,
@@ -1049,6 +1062,14 @@ void dispatch_bits_w(const ARParams& prm, const Plan& pl, bool one_shot, int64_t
     return;
   }
   if constexpr (sizeof(InT) == 2) {
+    if (prm.gs >= 16 && two_shot_stages() == 2) {  // 16 per lane, two stages per CTA
+      const int64_t u16 = prm.chunk / kUnit16;
+      if (pl.p1 == 16) launch_ar(two_shot16s_kernel<InT, OutT, 16, 16, WC>, prm, u16, W_emul, dev, st, kWarps16);
+      else if (pl.p1 == 8) launch_ar(two_shot16s_kernel<InT, OutT, 8, 8, WC>, prm, u16, W_emul, dev, st, kWarps16);
+      else if (pl.p2 == 8) launch_ar(two_shot16s_kernel<InT, OutT, 4, 8, WC>, prm, u16, W_emul, dev, st, kWarps16);
+      else launch_ar(two_shot16s_kernel<InT, OutT, 4, 4, WC>, prm, u16, W_emul, dev, st, kWarps16);
+      return;
+    }
     if (prm.gs >= 16) {  // 16 elements per lane: 512-element units
       const int64_t u16 = prm.chunk / kUnit16;
       if (pl.p1 == 16) launch_ar(two_shot16_kernel<InT, OutT, 16, 16, WC>, prm, u16, W_emul, dev, st, kWarps16);

@@ -613,7 +613,7 @@ void launch_norm(Kern kern, const ARNormParams& np, int W_emul, int dev, cudaStr
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, wpb * 32, 0);
   if (occ < 1) occ = 1;
   int64_t cap = (int64_t)occ * sms / std::max(1, W_emul);
-  cap = std::min<int64_t>(cap, multi ? (int64_t)kMaxBlocks : std::min<int64_t>(sms, kMaxBlocks));
+  cap = std::min<int64_t>(cap, multi ? (int64_t)kStageBlockOff : std::min<int64_t>(sms, kStageBlockOff));
   TORCH_CHECK(cap >= 1, "all_reduce_norm: no co-resident CTA budget (emulated world too large)");
   const int64_t G = std::max<int64_t>(1, std::min<int64_t>((np.R + wpb - 1) / wpb, cap));
   dim3 grid((unsigned)G, (unsigned)std::max(1, W_emul));
@@ -635,7 +635,7 @@ void launch_norm_rows(Kern kern, const ARNormParams& np, int W_emul, int dev, cu
   if (occ < 1) occ = 1;
   // every CTA must be resident at once (CTA b waits for CTA b of the other ranks)
   int64_t cap = (int64_t)occ * sms / std::max(1, W_emul);
-  cap = std::min<int64_t>(cap, (int64_t)kMaxBlocks);
+  cap = std::min<int64_t>(cap, (int64_t)kStageBlockOff);  // the two-shot family stays below the staged flags
   TORCH_CHECK(cap >= 1, "all_reduce_norm: no co-resident CTA budget (emulated world too large)");
   const int64_t G = std::max<int64_t>(1, std::min<int64_t>((np.R + rows_per_cta - 1) / rows_per_cta, cap));
   dim3 grid((unsigned)G, (unsigned)std::max(1, W_emul));

@@ -39,6 +39,7 @@ void quant_all_reduce_norm(const std::vector<std::shared_ptr<Workspace>>& wss, c
                            const std::vector<at::Tensor>& xs, int64_t bits, bool sym, bool scale_fp32,
                            bool quantize_local, double eps, double timeout_ms);
 int64_t set_norm_warps_per_row(int64_t wpr);
+int64_t set_two_shot_stages(int64_t stages);
 void gemm_all_reduce_norm(const std::shared_ptr<Workspace>& ws, const at::Tensor& a, const at::Tensor& w,
                           const at::Tensor& h, const at::Tensor& weight, at::Tensor& x, int64_t bits, bool sym,
                           bool scale_fp32, double eps, double timeout_ms);
@@ -148,6 +149,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "all_reduce(a @ w^T) with the quantize-and-scatter fused into the GEMM epilogue", py::arg("workspace"),
         py::arg("a"), py::arg("w"), py::arg("out"), py::arg("bits"), py::arg("group_size"), py::arg("sym"),
         py::arg("scale_fp32"), py::arg("timeout_ms"));
+  m.def("set_two_shot_stages", &qfc::set_two_shot_stages,
+        "stages per CTA of the 16-per-lane two-shot all-reduce (1 or 2); returns the previous value",
+        py::arg("stages"));
   m.def("set_norm_warps_per_row", &qfc::set_norm_warps_per_row,
         "warps per row of the sequence-parallel all-reduce + norm kernel (1, 2, 4 or 8); returns the previous value",
         py::arg("wpr"));

@@ -37,6 +37,10 @@ constexpr int64_t kFlagBytes = (int64_t)kFlagPhases * kMaxBlocks * kMaxRanks * s
 constexpr int64_t kArgmaxRows = 512;
 constexpr int64_t kArgmaxBytes = 2 * kMaxRanks * kArgmaxRows * 8;
 
+// The two-shot kernels' grids stay below this many CTAs; the staged two-shot kernel
+// publishes its second stage's flags at block index b + kStageBlockOff.
+constexpr int kStageBlockOff = kMaxBlocks / 2;
+
 // Two words of the one-shot epoch row that are not block epochs (the one-shot grid stays
 // below them): the rank's count of finished one-shot calls, whose parity selects the slot
 // region of a call, and the number of CTAs of the running call that have finished.

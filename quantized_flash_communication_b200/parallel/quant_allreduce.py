@@ -17,7 +17,8 @@ import torch.distributed as dist
 from .._ext import ext
 from .symm_mem import EmulatedWorkspaces, SymmetricWorkspace, default_timeout_ms
 
-__all__ = ["QuantAllReduce", "EmulatedQuantAllReduce", "ONE_SHOT_MAX_BYTES", "set_norm_warps_per_row"]
+__all__ = ["QuantAllReduce", "EmulatedQuantAllReduce", "ONE_SHOT_MAX_BYTES", "set_norm_warps_per_row",
+           "set_two_shot_stages"]
 
 # Messages up to this many input bytes use the one-shot algorithm under algo="auto".
 ONE_SHOT_MAX_BYTES = 512 * 1024
@@ -34,6 +35,14 @@ def set_norm_warps_per_row(wpr: int) -> int:
     value.  More than one warp per row multiplies the kernel's grid, for row counts per
     rank that leave SMs idle with one warp per row."""
     return int(ext().set_norm_warps_per_row(int(wpr)))
+
+
+def set_two_shot_stages(stages: int) -> int:
+    """Stages per CTA of the 16-per-lane two-shot all-reduce (1, or 2: each CTA's units in
+    two halves with their own flags, so that one half's waits and NVLink traffic overlap
+    the other half's work).  Process-wide, initially QFC_AR_STAGES or 1.  Returns the
+    previous value."""
+    return int(ext().set_two_shot_stages(int(stages)))
 
 
 def _pick_one_shot(algo: str, nbytes: int, one_shot_max: int) -> bool:

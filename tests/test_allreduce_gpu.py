@@ -50,9 +50,18 @@ CASES = [
 ]
 
 
+@pytest.fixture(params=[1, 2], ids=["stages1", "stages2"])
+def ar_stages(request):
+    """Stages per CTA of the 16-per-lane two-shot kernel (1: the default kernel)."""
+    from quantized_flash_communication_b200.parallel.quant_allreduce import set_two_shot_stages
+    prev = set_two_shot_stages(request.param)
+    yield request.param
+    set_two_shot_stages(prev)
+
+
 @pytest.mark.parametrize("W,bits,gs,mode,shape,algo", CASES)
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_emulated_matches_oracle(cuda_device, W, bits, gs, mode, shape, algo, dtype):
+def test_emulated_matches_oracle(cuda_device, ar_stages, W, bits, gs, mode, shape, algo, dtype):
     ar = EmulatedQuantAllReduce(W, cuda_device, bits=bits, group_size=gs, quant_type=mode, algo=algo,
                                 timeout_ms=5000)
     xs = _inputs(W, shape, dtype, cuda_device, seed=W * 100 + bits)
@@ -69,7 +78,7 @@ def test_emulated_matches_oracle(cuda_device, W, bits, gs, mode, shape, algo, dt
         xs = [x.roll(1) for x in xs]
 
 
-def test_sizes_change_between_calls(cuda_device):
+def test_sizes_change_between_calls(cuda_device, ar_stages):
     """One workspace, back-to-back calls whose sizes (and so grids) change, one-shot and
     two-shot interleaved: the one-shot slot region follows the rank's call count, the
     same in every block, so every call must still match the oracle on every rank."""

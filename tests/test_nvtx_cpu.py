@@ -1,6 +1,7 @@
 """Host-side switches of the native extension.  NVTX ranges: the switch reaches the
 extension, wrapped ops keep their signatures (keywords, defaults, in-place outputs) and
-an op's error still propagates.  The warps-per-row switch of the sequence-parallel kernel."""
+an op's error still propagates.  The warps-per-row switch of the sequence-parallel kernel
+and the stage switch of the two-shot kernel."""
 import pytest
 import torch
 
@@ -62,3 +63,14 @@ def test_norm_warps_per_row_switch():
         assert set_norm_warps_per_row(2) == 2
     finally:
         set_norm_warps_per_row(prev)
+
+
+def test_two_shot_stages_switch():
+    from quantized_flash_communication_b200.parallel.quant_allreduce import set_two_shot_stages
+    prev = set_two_shot_stages(2)
+    try:
+        assert set_two_shot_stages(1) == 2
+        with pytest.raises(RuntimeError):
+            set_two_shot_stages(3)
+    finally:
+        set_two_shot_stages(prev)
