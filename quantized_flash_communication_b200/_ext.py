@@ -21,7 +21,7 @@ _COUNTING = None  # dict name -> calls while counting
 # reduce kernel; decode attention launches its partial and merge kernels.
 _KERNELS_PER_CALL = {"attn_decode": 2, "quantize_cpu": 0, "dequantize_cpu": 0, "pack_int4_cpu": 0,
                      "unpack_int4_cpu": 0, "ar_plan": 0, "ar_plan_rows": 0, "gemm_status": 0, "attn_status": 0,
-                     "Workspace": 0, "set_nvtx": 0, "nvtx_enabled": 0, "set_norm_warps_per_row": 0, "set_attn_packed": 0, "set_two_shot_stages": 0, "gemm_all_reduce": 2, "gemm_all_reduce_norm": 2}
+                     "Workspace": 0, "set_nvtx": 0, "nvtx_enabled": 0, "set_norm_warps_per_row": 0, "set_attn_packed": 0, "set_two_shot_stages": 0, "set_gemv": 0, "gemm_all_reduce": 2, "gemm_all_reduce_norm": 2}
 
 
 def _load():

@@ -113,7 +113,12 @@ def main(argv=None):
     ap.add_argument("--breakdown", action="store_true",
                     help="also time eager decode steps per operator (CUDA-event regions, max over ranks)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--gemv", action="store_true",
+                    help="GEMMs of at most 8 rows on the weight-streaming kernel (set_gemv)")
     args = ap.parse_args(argv)
+    if args.gemv and args.impl == "ours":
+        from .._ext import ext
+        ext().set_gemv(True)
     rank, world, dev = init_distributed()
     cfg = get_config(args.model)
     if args.layers:
@@ -179,7 +184,8 @@ def main(argv=None):
             "benchmark": "tp_decode", "model": cfg.name, "n_gpus": world, "batch": B, "ctx": S, "new_tokens": args.new,
             "allreduce": f"{args.ar_backend} INT{args.bits} g{args.group_size}" if world > 1 else "none (tp1)",
             "ttft_ms": ttft, "per_token_ms": per_tok, "decode_tokens_per_s": B * 1000.0 / per_tok,
-            "launch": "cuda_graph", "clocks": sampler.summary() if sampler else None,
+            "launch": "cuda_graph", "small_m_gemm": "weight-streaming (gemv)" if args.gemv else "tcgen05",
+            "clocks": sampler.summary() if sampler else None,
             "eager_breakdown_ms_per_token": breakdown,
             "data": "synthetic: uniform random token ids, random-init N(0,0.02) weights"}), flush=True)
     reset_communicators()

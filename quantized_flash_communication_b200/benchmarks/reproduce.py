@@ -85,8 +85,9 @@ def items(gpus: int) -> Dict[str, List[Tuple[int, List[str]]]]:
         out["decode"].append((n, ["-m", f"{PKG}.bench_decode", "--model", "llama3-8b", "--batch", "64", "--ctx", "4096",
                                   "--new", "128", "--impl", "reference"]))
     if gpus >= 8:
-        out["decode"].append((8, ["-m", f"{PKG}.bench_decode", "--model", "llama3-70b", "--batch", "4", "--ctx", "2048",
-                                  "--new", "128", "--bits", "4"]))
+        for extra in ([], ["--gemv"]):
+            out["decode"].append((8, ["-m", f"{PKG}.bench_decode", "--model", "llama3-70b", "--batch", "4", "--ctx",
+                                      "2048", "--new", "128", "--bits", "4"] + extra))
     out["quant"] = [(1, ["-m", f"{PKG}.bench_quant", "--reference"])]
     probes = [["gemm"], ["attention", "8", "1024", "32", "32"], ["attention", "4", "2048", "64", "8"],
               ["attention", "2", "4096", "32", "8"], ["attention", "8", "1024", "32", "32", "--attn-packed"],

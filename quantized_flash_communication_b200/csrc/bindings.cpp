@@ -51,6 +51,7 @@ void gemm_qkv_rope(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, co
                    const c10::optional<at::Tensor>& v_cache, const c10::optional<at::Tensor>& slots, int64_t nq,
                    int64_t nkv, double timeout_ms);
 int64_t gemm_status(bool clear);
+bool set_gemv(bool on);
 // layers.cu
 void rmsnorm_cuda(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& y,
                   double eps);
@@ -120,6 +121,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("a"), py::arg("b"), py::arg("out") = py::none(), py::arg("epi") = 0,
         py::arg("residual") = py::none(), py::arg("timeout_ms") = 10000.0, py::arg("max_ctas") = 0);
   m.def("gemm_status", &qfc::gemm_status, py::arg("clear") = false);
+  m.def("set_gemv", &qfc::set_gemv,
+        "weight-streaming kernel for GEMMs of at most 8 rows (off by default); returns the previous value",
+        py::arg("on"));
   m.def("rmsnorm", qfc::traced("rmsnorm", &qfc::rmsnorm_cuda), py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("y"), py::arg("eps"));
   m.def("rope_kv_decode", qfc::traced("rope_kv_decode", &qfc::rope_kv_decode_cuda), "RoPE + paged KV write of one decode token per sequence");
   m.def("rope_kv", qfc::traced("rope_kv", &qfc::rope_kv_cuda), py::arg("qkv"), py::arg("pos"), py::arg("cos_sin"), py::arg("k_cache"),

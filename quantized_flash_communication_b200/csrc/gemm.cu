@@ -1184,6 +1184,10 @@ void launch_small(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, con
 }  // namespace small
 }  // namespace gemm
 
+// gemv.cu: the weight-streaming kernel for M <= 8 (opt-in); false when it does not apply.
+bool gemv_try(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi,
+              const c10::optional<at::Tensor>& residual);
+
 // out = a @ b^T (epi 0), silu(a @ gate^T) * (a @ up^T) with b = [gate; up] (epi 1),
 // a @ b^T + residual (epi 2).
 at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& out_opt, int64_t epi,
@@ -1208,6 +1212,7 @@ at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& b, const c10::option
     check_operand(*residual, "residual");
     TORCH_CHECK(residual->size(0) == M && residual->size(1) == N, "gemm: bad residual shape");
   }
+  if (max_ctas <= 0 && gemv_try(a, b, out, epi, residual)) return out;
   if (M <= small::TN && max_ctas <= 0 && (epi == EPI_STORE || epi == EPI_RESIDUAL) && small::small_enabled()) {
     small::launch_small(a, b, out, epi == EPI_RESIDUAL ? &*residual : nullptr, timeout_ms);
     return out;

@@ -74,3 +74,8 @@ def test_two_shot_stages_switch():
             set_two_shot_stages(3)
     finally:
         set_two_shot_stages(prev)
+
+
+def test_gemv_switch():
+    C.set_gemv(True)
+    assert C.set_gemv(False) is True
