@@ -1,7 +1,7 @@
 """Re-run the measurements behind the published tables with one command.
 
     python -m quantized_flash_communication_b200.benchmarks.reproduce --gpus 8 \
-        [--only flagship,variants,allreduce,norm,decode,quant,kernels] [--out results.jsonl] [--dry-run]
+        [--only flagship,variants,allreduce,norm,decode,tables,quant,kernels] [--out results.jsonl] [--dry-run]
 
 Every item is a list of commands: the benchmark modules of this package (one process
 per GPU under ``torch.distributed.run`` with the rendezvous on 127.0.0.1 when an item
@@ -20,6 +20,7 @@ Items (BASELINE.json configurations in brackets):
   norm       all-reduce + residual + RMSNorm: 1, 2, 4 warps per row      [3]
   decode     Llama-3-8B decode at TP 1, 2, 4, 8 (ours and reference), Llama-3-70B
              TP 8 INT4 prefill + decode                                  [4, 5]
+  tables     the reference's Tables 1-4 and its QA generation (main) at 1, 2, 4, 8
   quant      standalone quantizers vs the reference's                    [kernels]
   kernels    one kernel_probe line per hand-written kernel               [kernels]
 """
@@ -88,6 +89,7 @@ def items(gpus: int) -> Dict[str, List[Tuple[int, List[str]]]]:
         for extra in ([], ["--gemv"]):
             out["decode"].append((8, ["-m", f"{PKG}.bench_decode", "--model", "llama3-70b", "--batch", "4", "--ctx",
                                       "2048", "--new", "128", "--bits", "4"] + extra))
+    out["tables"] = [(n, ["-m", "quantized_flash_communication_b200.main", "--max-new-tokens", "32"]) for n in ns]
     out["quant"] = [(1, ["-m", f"{PKG}.bench_quant", "--reference"])]
     probes = [["gemm"], ["attention", "8", "1024", "32", "32"], ["attention", "4", "2048", "64", "8"],
               ["attention", "2", "4096", "32", "8"], ["attention", "8", "1024", "32", "32", "--attn-packed"],
@@ -114,7 +116,7 @@ def _run(cmd: List[str], timeout: float, env: Dict[str, str]) -> Tuple[int, str]
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--only", default="flagship,variants,allreduce,norm,decode,quant,kernels")
+    ap.add_argument("--only", default="flagship,variants,allreduce,norm,decode,tables,quant,kernels")
     ap.add_argument("--out", default="reproduce_results.jsonl")
     ap.add_argument("--timeout", type=float, default=300.0, help="seconds per command")
     ap.add_argument("--dry-run", action="store_true", help="print the commands only")

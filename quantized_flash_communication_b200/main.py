@@ -22,6 +22,7 @@ the tables and the QA generation test, and tears the process group down.
 from __future__ import annotations
 
 import argparse
+import json
 from typing import Dict, Optional, Sequence
 
 import torch
@@ -172,7 +173,10 @@ def main(argv=None):
     if rank == 0:
         print(f"model {cfg.name}: {cfg.num_layers} layers, hidden {cfg.hidden_size}, TP {world}")
     if not args.skip_tables:
-        benchmark_all_tables(model, None, device, rank)
+        tables = benchmark_all_tables(model, None, device, rank)
+        if rank == 0:  # one machine-readable line with every table's rows
+            print(json.dumps({"benchmark": "reference_tables", "model": cfg.name, "n_gpus": world, **tables}),
+                  flush=True)
     run_qa_test(model, None, device, rank, max_new_tokens=args.max_new_tokens)
     reset_communicators()
     cleanup_ddp()
