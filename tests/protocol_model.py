@@ -34,9 +34,13 @@ Protocols (``algo`` of a call):
                   when the grid changes between calls (a unit moves to a block whose epoch
                   has the other parity); the checker finds it, and the kernel uses the
                   call count instead.
+  two_shot_staged_offset  two_shot16s_kernel: each CTA's units in two stages, phase 1 of
+                  stage 1 issued before the wait for stage 0, stage 1's flags at the fixed
+                  block index b + STAGE_OFF of the same phases and epochs (every two-shot
+                  grid stays below STAGE_OFF; a grid that does not can collide, which the
+                  checker finds)
 Candidate schedules, checked before they are built:
-  two_shot_staged the two-shot units of each CTA in two stages with separate flag phases,
-                  phase 1 of stage 1 issued before the wait for stage 0
+  two_shot_staged the same schedule with stage 1's flags in separate flag phases
   two_shot_staged_shared  the same with stage 1's flags at block index b + G of the
                   stage-0 phase (unsafe: a flag word is then written under two different
                   blocks' epochs)
@@ -50,6 +54,11 @@ from typing import Callable, Dict, Iterator, List, Optional, Tuple
 
 class ProtocolViolation(AssertionError):
     pass
+
+
+# Block index of the staged kernel's second flag set (kStageBlockOff in the kernels, where
+# every two-shot grid is capped below it); the model's grids stay below this value.
+STAGE_OFF = 8
 
 
 @dataclass
@@ -118,6 +127,8 @@ class Model:
                 return (phase, b)
             if staged == "shared":  # stage 1 at block index b + G of the same phase
                 return (phase, b + G)
+            if staged == "offset":  # stage 1 at the fixed block index b + STAGE_OFF (the kernel's layout)
+                return (phase, b + STAGE_OFF)
             return (phase + "1", b)
 
         for s, us in enumerate(stages):          # phase 1 of every stage
@@ -282,6 +293,8 @@ class Model:
             return self._two_shot(r, k, call, b)
         if a == "two_shot_staged":
             return self._two_shot(r, k, call, b, staged="sep")
+        if a == "two_shot_staged_offset":
+            return self._two_shot(r, k, call, b, staged="offset")
         if a == "two_shot_staged_shared":
             return self._two_shot(r, k, call, b, staged="shared")
         if a == "one_shot":

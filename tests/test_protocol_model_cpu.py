@@ -27,7 +27,7 @@ def _violations(algo, seeds=SEEDS, capacity_choices=(None,), calls=6):
     return bad
 
 
-@pytest.mark.parametrize("algo", ["two_shot", "one_shot", "two_shot_staged"])
+@pytest.mark.parametrize("algo", ["two_shot", "one_shot", "two_shot_staged", "two_shot_staged_offset"])
 def test_protocol_has_no_race_or_deadlock(algo):
     assert _violations(algo) == 0
 
@@ -99,3 +99,31 @@ def test_checker_finds_a_missing_wait(algo, skip):
         except ProtocolViolation:
             bad += 1
     assert bad > len(SEEDS) // 4, bad
+
+
+def test_staged_and_plain_two_shot_share_flags_below_the_offset():
+    """Staged and one-stage two-shot calls interleaved on one workspace, every grid below
+    the stage offset: safe.  The same with one-stage grids reaching past the offset (its
+    CTAs then write the staged kernel's stage-1 flag words under their own epochs): the
+    checker must find the collision, which is why the kernels cap their grids."""
+    from protocol_model import STAGE_OFF
+
+    def run(max_grid_plain):
+        bad = 0
+        for seed in SEEDS:
+            rng = random.Random(seed)
+            calls = []
+            for _ in range(8):
+                if rng.random() < 0.5:
+                    units = rng.randint(1, 24)
+                    calls.append(Call("two_shot_staged_offset", units, rng.randint(1, min(6, units))))
+                else:
+                    units = rng.randint(1, 40)
+                    calls.append(Call("two_shot", units, rng.randint(1, min(max_grid_plain, units))))
+            try:
+                Model(rng.choice([2, 3, 4]), calls, seed=seed).run()
+            except ProtocolViolation:
+                bad += 1
+        return bad
+    assert run(STAGE_OFF) == 0
+    assert run(4 * STAGE_OFF) > 0
