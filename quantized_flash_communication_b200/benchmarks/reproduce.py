@@ -1,7 +1,7 @@
 """Re-run the measurements behind the published tables with one command.
 
     python -m quantized_flash_communication_b200.benchmarks.reproduce --gpus 8 \
-        [--only flagship,variants,allreduce,norm,decode,tables,quant,kernels] [--out results.jsonl] [--dry-run]
+        [--only flagship,variants,breakdown,allreduce,norm,decode,tables,quant,kernels] [--out results.jsonl] [--dry-run]
 
 Every item is a list of commands: the benchmark modules of this package (one process
 per GPU under ``torch.distributed.run`` with the rendezvous on 127.0.0.1 when an item
@@ -15,6 +15,7 @@ visible GPUs into ``<out>.clocks.csv`` (a failure to start it is reported, not f
 Items (BASELINE.json configurations in brackets):
   flagship   bench.py, ours and the reference arm, at 1, 2, 4, 8 GPUs   [3]
   variants   prefill step under each all-reduce variant at 2, 4, 8      [3]
+  breakdown  per-operator device time of the flagship step at 1, 2, 4, 8 [3]
   allreduce  all-reduce sweep vs NCCL bf16 at 2, 4, 8, and the reference's
              flash_all_reduce at group 128                               [2]
   norm       all-reduce + residual + RMSNorm: 1, 2, 4 warps per row      [3]
@@ -70,6 +71,7 @@ def items(gpus: int) -> Dict[str, List[Tuple[int, List[str]]]]:
         out["flagship"].append((n, ["bench.py", "--impl", "reference", "--gpus", str(n), "--steps", "5",
                                     "--warmup", "3"]))
     out["variants"] = [(n, ["-m", f"{PKG}.bench_prefill_variants", "--steps", "10", "--warmup", "3"]) for n in multi]
+    out["breakdown"] = [(n, ["bench.py", "--gpus", str(n), "--breakdown", "--steps", "3", "--warmup", "3"]) for n in ns]
     sweep = ["--tokens", "1,16,128,1024,4096,16384", "--hidden", "4096,8192", "--iters", "10"]
     out["allreduce"] = []
     for n in multi:
@@ -116,7 +118,7 @@ def _run(cmd: List[str], timeout: float, env: Dict[str, str]) -> Tuple[int, str]
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--only", default="flagship,variants,allreduce,norm,decode,tables,quant,kernels")
+    ap.add_argument("--only", default="flagship,variants,breakdown,allreduce,norm,decode,tables,quant,kernels")
     ap.add_argument("--out", default="reproduce_results.jsonl")
     ap.add_argument("--timeout", type=float, default=300.0, help="seconds per command")
     ap.add_argument("--dry-run", action="store_true", help="print the commands only")

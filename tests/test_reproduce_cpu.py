@@ -46,7 +46,8 @@ def _parser_of(target):
 @pytest.mark.parametrize("gpus", [1, 2, 8])
 def test_every_command_parses(gpus):
     table = reproduce.items(gpus)
-    assert set(table) == {"flagship", "variants", "allreduce", "norm", "decode", "tables", "quant", "kernels"}
+    assert set(table) == {"flagship", "variants", "breakdown", "allreduce", "norm", "decode", "tables", "quant",
+                          "kernels"}
     for item, cmds in table.items():
         for n, target in cmds:
             assert n <= gpus, (item, n)
