@@ -50,18 +50,9 @@ CASES = [
 ]
 
 
-@pytest.fixture(params=[1, 2], ids=["stages1", "stages2"])
-def ar_stages(request):
-    """Stages per CTA of the 16-per-lane two-shot kernel (1: the default kernel)."""
-    from quantized_flash_communication_b200.parallel.quant_allreduce import set_two_shot_stages
-    prev = set_two_shot_stages(request.param)
-    yield request.param
-    set_two_shot_stages(prev)
-
-
 @pytest.mark.parametrize("W,bits,gs,mode,shape,algo", CASES)
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_emulated_matches_oracle(cuda_device, ar_stages, W, bits, gs, mode, shape, algo, dtype):
+def test_emulated_matches_oracle(cuda_device, W, bits, gs, mode, shape, algo, dtype):
     ar = EmulatedQuantAllReduce(W, cuda_device, bits=bits, group_size=gs, quant_type=mode, algo=algo,
                                 timeout_ms=5000)
     xs = _inputs(W, shape, dtype, cuda_device, seed=W * 100 + bits)
@@ -78,7 +69,7 @@ def test_emulated_matches_oracle(cuda_device, ar_stages, W, bits, gs, mode, shap
         xs = [x.roll(1) for x in xs]
 
 
-def test_sizes_change_between_calls(cuda_device, ar_stages):
+def test_sizes_change_between_calls(cuda_device):
     """One workspace, back-to-back calls whose sizes (and so grids) change, one-shot and
     two-shot interleaved: the one-shot slot region follows the rank's call count, the
     same in every block, so every call must still match the oracle on every rank."""
@@ -177,19 +168,10 @@ def test_gemm_fused_scatter_single_rank(cuda_device, bits, mode):
         assert torch.equal(fused.cpu(), ref)
 
 
-@pytest.fixture(params=[1, 2, 4], ids=["wpr1", "wpr2", "wpr4"])
-def norm_wpr(request):
-    """Warps per row of the sequence-parallel kernel (1: one warp per row, the default)."""
-    from quantized_flash_communication_b200.parallel.quant_allreduce import set_norm_warps_per_row
-    prev = set_norm_warps_per_row(request.param)
-    yield request.param
-    set_norm_warps_per_row(prev)
-
-
 @pytest.mark.parametrize("W,M,H,bits,mode", [(2, 256, 1024, 8, "asym"), (4, 1000, 4096, 8, "asym"),
                                                (8, 300, 2048, 4, "sym"), (3, 77, 512, 6, "asym"),
                                                (2, 64, 256, 16, "asym"), (1, 130, 1024, 8, "asym")])
-def test_emulated_all_reduce_norm(cuda_device, norm_wpr, W, M, H, bits, mode):
+def test_emulated_all_reduce_norm(cuda_device, W, M, H, bits, mode):
     """Sequence-parallel all-reduce + residual + RMSNorm: residual shards bit-exact with the
     oracle, x identical on every rank and equal to the oracle up to rsqrt rounding."""
     from quantized_flash_communication_b200.parallel import EmulatedQuantAllReduce
@@ -214,7 +196,7 @@ def test_emulated_all_reduce_norm(cuda_device, norm_wpr, W, M, H, bits, mode):
         hs_in = h_ref  # the second call continues from the updated shards
 
 
-def test_gemm_fused_all_reduce_norm_single_rank(cuda_device, norm_wpr):
+def test_gemm_fused_all_reduce_norm_single_rank(cuda_device):
     """GEMM with the scatter epilogue + norm kernel == GEMM, then the norm all-reduce."""
     from quantized_flash_communication_b200.ops import gemm as G
     from quantized_flash_communication_b200.parallel import QuantAllReduce

@@ -19,19 +19,9 @@ def _ref(qkv, B, S, nq, nkv, hd):
     return (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B * S, nq * hd)
 
 
-@pytest.fixture(params=[False, True], ids=["scalar", "packed"])
-def softmax_form(request):
-    """Both softmax forms of the kernel: scalar fp32 arithmetic (the default) and the packed
-    two-lane fp32 instructions (set_attn_packed)."""
-    from quantized_flash_communication_b200._ext import ext
-    prev = ext().set_attn_packed(request.param)
-    yield request.param
-    ext().set_attn_packed(prev)
-
-
 @pytest.mark.parametrize("B,S,nq,nkv", [(1, 128, 1, 1), (2, 100, 4, 4), (2, 300, 8, 2), (1, 1024, 4, 1), (3, 100, 8, 4),
                                          (3, 257, 2, 2), (8, 1024, 4, 4)])
-def test_prefill_attention_matches_reference(cuda_device, softmax_form, B, S, nq, nkv):
+def test_prefill_attention_matches_reference(cuda_device, B, S, nq, nkv):
     hd = 128
     torch.manual_seed(B * S + nq)
     qkv = torch.randn(B * S, (nq + 2 * nkv) * hd, device=cuda_device, dtype=torch.bfloat16)
@@ -57,14 +47,10 @@ def test_fma_pipe_exp2_against_exp2f(cuda_device):
     y2 = torch.empty(1, device=cuda_device)
     ext().attn_exp2_poly(torch.tensor([float("-inf")], device=cuda_device), y2)
     assert 0 <= y2.item() < 1e-37
-    # the packed two-lane form rounds exactly like the scalar one, lane by lane
-    yp = torch.empty_like(x)
-    ext().attn_exp2_poly(x, yp, pairs=True)
-    assert torch.equal(yp.view(torch.int32), y.view(torch.int32))
 
 
 @pytest.mark.parametrize("B,S,nq,nkv", [(2, 1024, 4, 4), (1, 2048, 8, 2)])
-def test_prefill_attention_row_maxima_that_grow(cuda_device, softmax_form, B, S, nq, nkv):
+def test_prefill_attention_row_maxima_that_grow(cuda_device, B, S, nq, nkv):
     """Keys whose scale grows along the sequence make the running maximum of some rows (not
     all) jump by more than 2^8 between tiles: the lazy O rescale runs for part of a warp."""
     hd = 128

@@ -107,49 +107,3 @@ def test_gemm_persistent_small_grid(cuda_device):
     y = ext().gemm_bf16(a, b, None, 0, None, 10000.0, 3)  # 3 CTAs loop over 32 tiles
     _check(y, _ref(a, b), _sigma(a, b), what="3-CTA persistent")
 
-
-@pytest.fixture
-def gemv_on():
-    """The weight-streaming kernel for at most 8 rows (off by default)."""
-    from quantized_flash_communication_b200._ext import ext
-    prev = ext().set_gemv(True)
-    yield
-    ext().set_gemv(prev)
-
-
-@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (3, 300, 1000), (4, 1280, 8192), (8, 4096, 4096), (5, 9, 2056)])
-def test_gemv_store_and_residual(cuda_device, gemv_on, M, N, K):
-    """M <= 8 through the weight-streaming kernel: the same bounds as the tensor-core path."""
-    torch.manual_seed(M * N + K)
-    a = torch.randn(M, K, device=cuda_device, dtype=torch.bfloat16)
-    b = torch.randn(N, K, device=cuda_device, dtype=torch.bfloat16) * 0.05
-    s = _sigma(a, b)
-    ab = _ref(a, b)
-    _check(G.linear(a, b), ab, s, what=f"gemv {M}x{N}x{K}")
-    r = torch.randn(M, N, device=cuda_device, dtype=torch.bfloat16)
-    ref = _bf16(ab) + r.float()
-    G.linear_residual(a, b, r, out=r)
-    torch.cuda.synchronize()
-    _check(r, ref, s, what=f"gemv residual {M}x{N}x{K}", extra=2.0 ** -7 * ab.abs())
-
-
-@pytest.mark.parametrize("M,I,K", [(1, 128, 64), (4, 3584, 8192), (7, 1376, 4096)])
-def test_gemv_swiglu(cuda_device, gemv_on, M, I, K):
-    torch.manual_seed(I + M)
-    a = torch.randn(M, K, device=cuda_device, dtype=torch.bfloat16)
-    w = torch.randn(2 * I, K, device=cuda_device, dtype=torch.bfloat16) * 0.03
-    y = G.linear_swiglu(a, w)
-    torch.cuda.synchronize()
-    g = _bf16(_ref(a, w[:I]))
-    u = _bf16(_ref(a, w[I:]))
-    ref = _bf16(torch.nn.functional.silu(g)) * u
-    s = _sigma(a, w)
-    extra = 2.0 ** -6 * (g.abs() + 1.0) * u.abs()
-    _check(y, ref, s * s, rel=2.0 ** -7, what=f"gemv swiglu {M}x{I}x{K}", extra=extra)
-
-
-def test_gemv_declines_what_it_cannot_do(cuda_device, gemv_on):
-    """More than 8 rows, or K not a multiple of 8: the tensor-core path runs instead."""
-    a = torch.randn(9, 512, device=cuda_device, dtype=torch.bfloat16)
-    b = torch.randn(256, 512, device=cuda_device, dtype=torch.bfloat16) * 0.05
-    _check(G.linear(a, b), _ref(a, b), _sigma(a, b), what="9 rows")
