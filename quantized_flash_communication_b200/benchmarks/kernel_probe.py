@@ -16,6 +16,9 @@
     python -m quantized_flash_communication_b200.benchmarks.kernel_probe gemm_small 64 4096 14336
     python -m quantized_flash_communication_b200.benchmarks.kernel_probe qkv_rope 8192 4096 32 32
 
+Switches of the opt-in kernels: --attn-packed (attention), --stages 2 (allreduce),
+--norm-wpr 2|4|8 (allreduce_norm), --gemv (gemm / gemm_small with M <= 8).
+
 Each subcommand runs ``--iters`` launches (default 3) after one warm-up and prints the
 median device time; ``allreduce`` and ``allreduce_norm`` (the sequence-parallel
 all-reduce + residual + RMSNorm) run W ranks emulated inside one launch on one GPU.
@@ -39,10 +42,16 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--attn-packed", action="store_true",
                     help="attention: the softmax with packed two-lane fp32 arithmetic")
+    ap.add_argument("--stages", type=int, default=1, help="allreduce: stages per CTA of the two-shot kernel (1, 2)")
+    ap.add_argument("--norm-wpr", type=int, default=1, help="allreduce_norm: warps per row (1, 2, 4, 8)")
+    ap.add_argument("--gemv", action="store_true", help="gemm / gemm_small: the weight-streaming kernel (M <= 8)")
     args = ap.parse_args(argv)
-    if args.attn_packed:
+    if args.attn_packed or args.stages != 1 or args.norm_wpr != 1 or args.gemv:
         from .._ext import ext
-        ext().set_attn_packed(True)
+        ext().set_attn_packed(args.attn_packed)
+        ext().set_two_shot_stages(args.stages)
+        ext().set_norm_warps_per_row(args.norm_wpr)
+        ext().set_gemv(args.gemv)
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
     if args.kernel == "gemm":

@@ -96,7 +96,9 @@ def items(gpus: int) -> Dict[str, List[Tuple[int, List[str]]]]:
     probes = [["gemm"], ["attention", "8", "1024", "32", "32"], ["attention", "4", "2048", "64", "8"],
               ["attention", "2", "4096", "32", "8"], ["attention", "8", "1024", "32", "32", "--attn-packed"],
               ["attention", "4", "2048", "64", "8", "--attn-packed"], ["allreduce", "2", "16384", "4096", "8"],
-              ["allreduce_norm", "8", "8192", "4096", "8"], ["quantize"], ["decode"], ["rmsnorm"], ["rope_decode"],
+              ["allreduce", "8", "8192", "4096", "8"], ["allreduce", "8", "8192", "4096", "8", "--stages", "2"],
+              ["allreduce_norm", "8", "8192", "4096", "8"], ["allreduce_norm", "8", "8192", "4096", "8", "--norm-wpr", "4"],
+              ["gemm_small", "4", "8192", "8192"], ["gemm_small", "4", "8192", "8192", "--gemv"], ["quantize"], ["decode"], ["rmsnorm"], ["rope_decode"],
               ["silu_mul"], ["pack"], ["unpack"], ["oneshot"], ["gemm_qs8"], ["gemm_small"], ["qkv_rope"]]
     out["kernels"] = [(1, ["-m", f"{PKG}.kernel_probe"] + p + ["--iters", "10"]) for p in probes]
     return out
