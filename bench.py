@@ -232,10 +232,18 @@ def _breakdown(args, model, tp, ids, cache, dev, rank, world):
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     if rank == 0:
+        from quantized_flash_communication_b200.benchmarks.roofline import fractions, op_bounds
         out = {n: round(float(v), 4) for n, v in zip(names, vals[:-1].tolist())}
+        counts = {n: summ[n]["count"] // args.steps for n in names}
+        peak_tf, hbm_gbs, peak_src = _peaks()
+        B, S = ids.shape
+        bounds = op_bounds(model.cfg, B, S, world, args.bits, args.group_size, peak_tf, hbm_gbs)
         print(json.dumps({"breakdown_ms_per_step_max_over_ranks": out, "eager_ms_per_step": float(vals[-1]),
                           "n_gpus": world, "fuse_gemm": not args.no_fuse_gemm, "ar_backend": args.ar_backend,
-                          "counts_per_step": {n: summ[n]["count"] // args.steps for n in names}}), flush=True)
+                          "counts_per_step": counts,
+                          "roofline_per_region": fractions(out, counts, bounds),
+                          "roofline_peaks": f"{peak_src}: {peak_tf} TFLOP/s bf16 sustained, {hbm_gbs} GB/s copy, "
+                                            "770 GB/s NVLink per direction"}), flush=True)
     return None
 
 
