@@ -124,8 +124,12 @@ def main(argv=None) -> int:
     ap.add_argument("--out", default="reproduce_results.jsonl")
     ap.add_argument("--timeout", type=float, default=300.0, help="seconds per command")
     ap.add_argument("--dry-run", action="store_true", help="print the commands only")
+    ap.add_argument("--ns", default="", help="run only the commands for these GPU counts, e.g. 8 or 2,4")
     args = ap.parse_args(argv)
     table = items(args.gpus)
+    if args.ns:
+        keep = {int(v) for v in args.ns.split(",") if v}
+        table = {k: [(n, t) for n, t in v if n in keep] for k, v in table.items()}
     wanted = [w for w in args.only.split(",") if w]
     unknown = [w for w in wanted if w not in table]
     if unknown:

@@ -66,3 +66,9 @@ def test_dry_run_lists_commands(capsys):
     assert reproduce.main(["--gpus", "2", "--only", "flagship,quant", "--dry-run"]) == 0
     out = capsys.readouterr().out.splitlines()
     assert any("bench.py --gpus 2" in ln for ln in out) and any("bench_quant" in ln for ln in out)
+
+
+def test_gpu_count_filter(capsys):
+    assert reproduce.main(["--gpus", "8", "--only", "variants,flagship", "--ns", "8", "--dry-run"]) == 0
+    out = capsys.readouterr().out.splitlines()
+    assert out and all("--nproc-per-node=8" in ln for ln in out)
