@@ -136,12 +136,12 @@ def main(argv=None) -> int:
         ap.error(f"unknown items {unknown}; choose from {sorted(table)}")
     env = dict(os.environ)
     env.setdefault("QFC_COMM_TIMEOUT_MS", "3000")  # bounded waits end a stuck rank quickly
-    smi = None
+    smi = smi_log = None
     if not args.dry_run:
         try:
+            smi_log = open(args.out + ".clocks.csv", "w")
             smi = subprocess.Popen(["nvidia-smi", f"--query-gpu={SMI_QUERY}", "--format=csv", "-lms", "500"],
-                                   stdout=open(args.out + ".clocks.csv", "w"), stderr=subprocess.STDOUT,
-                                   start_new_session=True)
+                                   stdout=smi_log, stderr=subprocess.STDOUT, start_new_session=True)
         except OSError as e:
             print(f"clock sampler not started: {e}", file=sys.stderr)
     failures = 0
@@ -171,6 +171,9 @@ def main(argv=None) -> int:
     finally:
         if smi is not None:
             os.killpg(smi.pid, signal.SIGTERM)
+            smi.wait(timeout=10)
+        if smi_log is not None:
+            smi_log.close()
     return 1 if failures else 0
 
 
