@@ -665,7 +665,8 @@ class LlamaTP(nn.Module):
     @torch.no_grad()
     def generate(self, ids: torch.Tensor, max_new_tokens: int, cache: Optional[KVCache] = None,
                  do_sample: bool = False, temperature: float = 1.0, top_p: float = 1.0,
-                 seed: Optional[int] = None, sampler: Optional[Sampler] = None) -> torch.Tensor:
+                 seed: Optional[int] = None, sampler: Optional[Sampler] = None, monitor=None,
+                 check_every: int = 16) -> torch.Tensor:
         """Generate ``max_new_tokens`` tokens per sequence; returns them as [B, max_new_tokens].
 
         Greedy by default.  ``do_sample=True`` samples from softmax(logits / temperature),
@@ -673,7 +674,17 @@ class LlamaTP(nn.Module):
         ``generate``, which the reference calls with ``do_sample=True, temperature=0.7``).
         Every rank draws the same tokens: the seed is rank 0's (``seed`` or a random one),
         broadcast once.  Collective: all ranks of the group call it together.
+
+        ``monitor`` (``utils.health.PeerMonitor``): before the prefill and every
+        ``check_every`` decode steps the stream is synchronised and the peers' heartbeats
+        checked, so that a lost rank raises ``PeerLostError`` on the host instead of the
+        next step's collectives waiting out their device timeout.
         """
+        def check():
+            if monitor is not None:
+                torch.cuda.current_stream(self.device).synchronize()
+                monitor.check()
+
         if sampler is None and do_sample:
             sampler = Sampler(self.tp, temperature=temperature, top_p=top_p, seed=seed)
         B, S = ids.shape
@@ -682,9 +693,12 @@ class LlamaTP(nn.Module):
         if S + max_new_tokens - 1 > cache.capacity:
             raise ValueError(f"cache holds {cache.capacity} tokens per sequence; {S} + {max_new_tokens} requested")
         out = torch.empty(B, max_new_tokens, dtype=torch.int64, device=self.device)
+        check()
         tok = self.prefill(ids, cache, sampler=sampler)
         out[:, 0] = tok
         for t in range(1, max_new_tokens):
+            if t % check_every == 0:
+                check()
             tok = self.decode_step(tok, cache, sampler)
             out[:, t] = tok
         return out
