@@ -40,3 +40,12 @@ def test_fractions_skip_unbounded_regions():
     fr = fractions({"attention": 2.0, "  (gemm part)": 1.0}, {"attention": 32, "  (gemm part)": 64},
                    {"attention": 0.05})
     assert fr == {"attention": {"bound_ms_per_step": 1.6, "fraction": 0.8}}
+
+
+def test_allreduce_sweep_uses_the_same_link_bytes():
+    """bench_allreduce's roofline and the step's share one formula for the two-shot."""
+    from quantized_flash_communication_b200.benchmarks.bench_allreduce import _wire_bytes
+    for n, W, bits, gs in [(4096 * 16384, 8, 8, 128), (4096 * 1024, 4, 4, 32), (8192 * 4096, 2, 6, 64)]:
+        assert _wire_bytes(n, W, bits, gs, False) == pytest.approx(allreduce_link_bytes(n, W, bits, gs))
+    # one-shot: every rank pushes its whole quantized tensor to each of the W - 1 peers
+    assert _wire_bytes(4096, 8, 8, 128, True) == pytest.approx(7 * 4096 * (1 + 4 / 128))
