@@ -51,3 +51,18 @@ def test_tp_shards_tile_the_full_weights():
         assert torch.equal(torch.cat([s[k] for s in shards], 1), full[k])
     assert torch.equal(torch.cat([s["lm_head.weight"] for s in shards], 0)[:cfg.vocab_size], full["lm_head.weight"])
     assert torch.equal(shards[1]["model.embed_tokens.weight"], full["model.embed_tokens.weight"])
+
+
+def test_configs_match_the_benchmark_configurations():
+    """The architectures the benchmarks run are the ones the benchmark configurations name:
+    Llama-2-7B (32 layers, hidden 4096, 32 heads, FFN 11008, vocab 32000), Llama-3-8B
+    (32 / 4096 / 32 q + 8 kv heads / 14336 / 128256) and Llama-3-70B (80 / 8192 / 64 + 8 /
+    28672 / 128256); head_dim 128 everywhere, and every head count divides by 8 ranks."""
+    from quantized_flash_communication_b200.models.config import get_config
+    want = {"llama2-7b": (32, 4096, 32, 32, 11008, 32000), "llama3-8b": (32, 4096, 32, 8, 14336, 128256),
+            "llama3-70b": (80, 8192, 64, 8, 28672, 128256)}
+    for name, (L, H, nq, nkv, inter, vocab) in want.items():
+        c = get_config(name)
+        assert (c.num_layers, c.hidden_size, c.num_heads, c.num_kv_heads, c.intermediate_size,
+                c.vocab_size) == (L, H, nq, nkv, inter, vocab), name
+        assert c.head_dim == 128 and nq % 8 == 0 and nkv % 8 == 0 and inter % 8 == 0, name
